@@ -1,0 +1,184 @@
+"""Pins the CPU oracle: the reference's own known-answer tests, and the golden
+fixtures that tests/golden/make_golden.py produced by running the reference's
+unchanged Python frontend (nn/optim/distributed) on the restated backend.
+
+The oracle is the checker for every GPU parity test, so these run first and
+on CPU only.
+"""
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from oracle.orca_shim import Tensor
+from orcaml_b200.synthetic import init_params, make_batch
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def bits(v):
+    return np.float32(v).view(np.uint32).tobytes().hex()
+
+
+def digest(params):
+    h = hashlib.sha256()
+    for p in params:
+        h.update(np.ascontiguousarray(p, np.float32).tobytes())
+    return h.hexdigest()
+
+
+# ---- reference known-answer tests ----------------------------------------------
+def test_kat_autograd_matmul():
+    """orca-autograd/tests/autograd_tests.rs:6-52: y = x@w, loss=(y-10)^2 -> dW = [-20,-30]."""
+    x = Tensor.from_list([2.0, 3.0], shape=[1, 2], requires_grad=True)
+    w = Tensor.from_list([1.0, 1.0], shape=[2, 1], requires_grad=True)
+    y = x @ w
+    diff = y - Tensor.from_list([10.0], shape=[1, 1])
+    loss = diff * diff
+    loss.backward()
+    assert w.grad().to_list() == [-20.0, -30.0]
+
+
+def test_kat_relu():
+    """autograd_tests.rs:55-90: relu([-1,2]) = [0,2], grad [0,1]."""
+    x = Tensor.from_list([-1.0, 2.0], shape=[1, 2], requires_grad=True)
+    y = x.relu()
+    assert y.to_list() == [0.0, 2.0]
+    (y * Tensor.from_list([1.0, 1.0], shape=[1, 2])).backward()
+    assert x.grad().to_list() == [0.0, 1.0]
+
+
+def test_kat_square_and_poly():
+    """python/tests/test_api.py:53-61 and 196-218."""
+    x = Tensor.from_list([2.0], shape=[1, 1], requires_grad=True)
+    (x * x).backward()
+    assert abs(x.grad().to_list()[0] - 4.0) < 1e-5
+    x = Tensor.from_list([2.0], shape=[1], requires_grad=True)
+    y = x * x * x + x * x * Tensor.scalar(2.0) + x * Tensor.scalar(5.0)
+    y.backward()
+    assert abs(x.grad().to_list()[0] - 25.0) < 1e-2
+
+
+def test_kat_cross_entropy_value():
+    """test_api.py:83-89: CE([1,0] vs one-hot [1,0]) = ln(1 + e^-1) > 0."""
+    loss, _ = O.softmax_ce(np.array([[1.0, 0.0]], np.float32), np.array([[1.0, 0.0]], np.float32))
+    assert loss > 0.0
+    assert abs(loss - np.log1p(np.exp(-1.0))) < 1e-6
+
+
+def test_kat_linear_numerical_gradient():
+    """test_api.py:250-279: d(x@W)/dW[0] = x[0] = 1.5."""
+    x = Tensor.from_list([1.5, -2.0], shape=[1, 2])
+    W = Tensor.from_list([0.8, 1.2], shape=[2, 1], requires_grad=True)
+    (x @ W).backward()
+    assert abs(W.grad().to_list()[0] - 1.5) < 1e-3
+
+
+def test_kat_ddp_identical_ranks():
+    """python/tests/test_phase8.py:109-164: Linear(3,3) with weights and bias 0.1,
+    x = [[1,2,3],[4,5,6]], loss = out.sum(); two ranks on identical data average
+    to their local gradients (within 1e-5; exactly here)."""
+    x = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    w = np.full((3, 3), 0.1, np.float32)
+    g_out = np.ones((2, 3), np.float32)
+    dW = O.matmul(O.transpose(x, [2, 3], 0, 1), g_out)
+    db = O.sum_to_shape(g_out, [2, 3], [1, 3])
+    assert dW.tolist() == [[5.0] * 3, [7.0] * 3, [9.0] * 3]
+    assert db.tolist() == [[2.0, 2.0, 2.0]]
+    for g in (dW, db):
+        avg = O.ddp_average([g, g])
+        np.testing.assert_allclose(avg, g, atol=1e-5)
+        assert np.array_equal(avg, g)
+    del w
+
+
+def test_kat_chunk_grads_via_sum_to_shape():
+    """test_api.py:323-346 backward ends in sum_to_shape([1]) -> expand; grads
+    [10,20,30,10,20,30] come from mul_scalar over expanded ones."""
+    g = O.expand(np.array([1.0], np.float32), [1], [2, 3])
+    assert g.tolist() == [[1.0] * 3] * 2
+
+
+# ---- primitive semantics ----------------------------------------------------------
+def test_log_clamp_and_unclamped_backward():
+    """backend.rs:577 clamps at 1e-7; log_backward (:629) does not."""
+    out = O.log(np.array([0.0, -1.0, 1e-8, 1.0], np.float32))
+    assert np.all(out[:3] == np.float32(np.log(np.float32(1e-7))))
+    assert out[3] == 0.0
+    g = O.log_backward(np.ones(2, np.float32), np.array([2.0, 0.0], np.float32))
+    assert g[0] == 0.5 and np.isinf(g[1])
+
+
+def test_sum_to_shape_serial_order():
+    """sum_to_shape adds in ascending linear order from 0 (backend.rs:519-527)."""
+    a = np.array([[1e8, 1.0, -1e8, 1.0]], np.float32).T  # [4,1]
+    s = O.sum_to_shape(a, [4, 1], [1, 1])
+    ref = np.float32(0)
+    for v in a[:, 0]:
+        ref = np.float32(ref + v)
+    assert s[0, 0] == ref
+
+
+def test_max_ties_all_receive_grad():
+    """max_to_shape_backward gives every tied maximum the gradient (backend.rs:1421)."""
+    p = np.array([[1.0, 3.0, 3.0]], np.float32)
+    m = O.max_to_shape(p, [1, 3], [1, 1])
+    g = O.max_to_shape_backward(np.array([[2.0]], np.float32), p, m, [1, 3], [1, 1])
+    assert g.tolist() == [[0.0, 2.0, 2.0]]
+
+
+def test_matmul_against_float64():
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((37, 53)).astype(np.float32)
+    b = rng.standard_normal((53, 29)).astype(np.float32)
+    c = O.matmul(a, b)
+    np.testing.assert_allclose(c, a.astype(np.float64) @ b.astype(np.float64), rtol=1e-5, atol=1e-5)
+
+
+def test_transpose_roundtrip():
+    a = np.arange(24, dtype=np.float32).reshape(2, 3, 4)
+    t = O.transpose(a, [2, 3, 4], 0, 2)
+    assert np.array_equal(t, np.transpose(a, (2, 1, 0)))
+
+
+# ---- golden fixtures from the reference's own Python -----------------------------
+CASES = ["c0", "sgdm_small", "sgd_small", "adamw_ddp2_small", "c1_ddp2_mid"]
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_matches_reference_golden(golden, name):
+    case = golden[name]
+    dims = case["dims"]
+    world = case.get("world", 1)
+    tr = O.OracleTrainer(dims, init_params(dims, 1), optimizer=case["optimizer"], lr=case["lr"],
+                         momentum=case.get("momentum", 0.0),
+                         weight_decay=case.get("weight_decay", 0.0))
+    batches = [make_batch(dims, case["batch"], r) for r in range(world)]
+    losses = [[] for _ in range(world)]
+    for _ in range(case["steps"]):
+        if world == 1:
+            losses[0].append(bits(tr.step(batches[0][0], batches[0][1])))
+        else:
+            ls = tr.step_ddp([b[0] for b in batches], [b[1] for b in batches])
+            for r, l in enumerate(ls):
+                losses[r].append(bits(l))
+    assert losses == case["loss_bits"]
+    assert digest(tr.params) == case["final"]["sha256"]
+    _, logits = O.mlp_forward(dims, tr.params, batches[0][0], batches[0][1])
+    assert [int(v) for v in np.argmax(logits, axis=1)] == case["argmax"]
+    path = os.path.join(GOLD, f"{name}_final.npz")
+    if os.path.exists(path):
+        ref = np.load(path)
+        for i, p in enumerate(tr.params):
+            assert np.array_equal(p, ref[f"arr_{i}"])
+
+
+def test_oracle_ce_ties_golden(golden):
+    case = golden["ce_ties"]
+    P = np.array(case["P"], np.float32)
+    T = np.array(case["T"], np.float32)
+    loss, dP = O.softmax_ce(P, T)
+    assert bits(loss) == case["loss_bits"]
+    assert [bits(v) for v in dP.reshape(-1)] == case["dP_bits"]
