@@ -1,0 +1,315 @@
+"""Benchmark: train samples/s of MLP 784-8192-8192-10 FP32 data-parallel
+training (SGD momentum 0.9, lr 0.01, per-rank batch
+4096) on N B200s, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one full training step (forward, softmax-CE, backward, NCCL
+all-reduce of the gradients when N > 1, optimizer update).  Every rank holds a
+full replica and its own batch (weak scaling); `value` counts samples of all
+ranks.  Timing: W untimed steps, then K steps bracketed by a barrier and a
+device synchronise on both sides, timed with CUDA events on the library's
+compute stream, max over ranks.  The step's working set (the 8192x8192
+weight planes alone are 512 MB) exceeds the 126 MB L2, so no flush is needed.
+
+`--impl reference` times the reference's CPU path restated in oracle/ (the
+Rust reference cannot be built here) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from orcaml_b200.synthetic import CONFIGS, init_params, make_batch  # noqa: E402
+
+CFG = CONFIGS["c2"]
+METRIC = "train samples/s, MLP 784-8192-8192-10 FP32 DDP (SGD momentum 0.9, per-rank batch 4096)"
+UNIT = "samples/s"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(steps=1, batch=64, warmup=0):
+    """The reference's CPU path (oracle/, restating orca-backend-cpu + the
+    Python frontend) on a bounded sample: `batch` rows of the configs[2]
+    model per step, all host threads for the element-wise loops, the GEMM
+    single-threaded like the reference's matrixmultiply."""
+    from oracle import oracle as O
+    O.set_threads(0)
+    dims = CFG.dims
+    tr = O.OracleTrainer(dims, init_params(dims, 1), optimizer="sgd", lr=CFG.lr,
+                         momentum=CFG.momentum)
+    x, t, _ = make_batch(dims, batch, 0)
+    for _ in range(warmup):
+        tr.step(x, t)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tr.step(x, t)
+    dt = time.perf_counter() - t0
+    return {"value": steps * batch / dt, "unit": UNIT, "cores": O.threads(),
+            "kind": "port",
+            "sample": f"{steps} step(s) of the 784-8192-8192-10 SGD-momentum step at batch {batch} "
+                      f"(of 4096): GEMM single-threaded, element-wise loops on {O.threads()} threads",
+            "seconds": dt}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    batch = 64
+    t0 = time.perf_counter()
+    cpu_baseline(steps=max(args.warmup, 0), batch=batch) if args.warmup else None
+    res = cpu_baseline(steps=args.steps, batch=batch)
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * res["seconds"] / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "784-8192-8192-10 SGD momentum 0.9 step, CPU, "
+                                   f"bounded sample of {batch} rows per step",
+                       "global_batch": batch, "parallelism": "single process (rank 0)"},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t0}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from orcaml_b200.backend import CudaBackend
+    from orcaml_b200.distributed import NcclCommunicator, nccl_unique_id
+    from orcaml_b200.mlp import MlpTrainer
+
+    be = CudaBackend(local)
+    B = CFG.batch
+    tr = MlpTrainer(be, CFG.dims, B, optimizer="sgd", lr=CFG.lr, momentum=CFG.momentum)
+    tr.set_parameters(init_params(CFG.dims, 1))
+    comm = None
+    if world > 1:
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = NcclCommunicator(be, rank, world, obj[0], timeout=120.0)
+        tr.attach_comm(comm, bucket_bytes=args.bucket_mb << 20)
+
+    x, t, _ = make_batch(CFG.dims, B, rank)
+    xs = be.from_f32_slice(list(x.shape), x)
+    ts = be.from_f32_slice(list(t.shape), t)
+    loss_s = be.zeros([1])
+    stream = torch.cuda.ExternalStream(be.stream_handle(), device=torch.device("cuda", local))
+
+    def barrier():
+        be.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(local)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        tt = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    # ---- device-resident step (value) ----
+    for _ in range(args.warmup):
+        tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+    barrier()
+    launches0 = be.launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        ev0.record(stream)
+        tr.profile_begin()
+        for _ in range(args.steps):
+            tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+        ev1.record(stream)
+        sites = tr.profile_end()
+        barrier()
+    launches = be.launch_count() - launches0
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_step = ms / args.steps
+    value = world * B * args.steps / (ms / 1000.0)
+    loss_val = float(be.to_f32_vec(loss_s)[0])
+
+    # ---- end to end through the host API: pinned inputs, H2D + D2H inside ----
+    xp = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
+    tp = torch.empty(t.shape, dtype=torch.float32, pin_memory=True)
+    xp.numpy()[:] = x
+    tp.numpy()[:] = t
+    host_loss = ctypes.c_float()
+    for _ in range(max(1, args.warmup // 2)):
+        tr.step_host_ptr(xp.data_ptr(), tp.data_ptr(), host_loss)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        tr.step_host_ptr(xp.data_ptr(), tp.data_ptr(), host_loss)   # reads the loss back
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = world * B * args.steps / (e2e_ms / 1000.0)
+
+    # ---- roofline of the dominant kernel: the tcgen05 GEMM ----
+    peaks, peak_src = load_peaks()
+    tf32_peak = peaks["bf16_tflops"] / 2.0 / 3.0    # FP32-equivalent rate of 3xTF32
+    tc_sites = [s for s in sites if s["gemm_path"] == 2]
+    tc_ms = sum(s["ms"] for s in tc_sites)
+    tc_flops = sum(s["flops"] * s["launches"] for s in tc_sites)
+    tc_launches = sum(s["launches"] for s in tc_sites)
+    achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
+    step_flops = CFG.flops_per_sample() * B
+    breakdown = {s["name"]: round(s["ms"] / max(1, s["launches"]), 4) for s in sites}
+
+    result = None
+    if rank == 0:
+        cpu = cpu_baseline(steps=1, batch=128) if (world == 1 and not args.no_cpu) else None
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (uniform [0,1) inputs seed=rank, uniform labels, "
+                    "Kaiming-uniform weights seed 1)",
+            "config": {"workload": "BASELINE configs[2]: MLP 784-8192-8192-10, SGD momentum 0.9 "
+                                   "lr 0.01, per-rank batch 4096",
+                       "global_batch": world * B, "per_rank_batch": B,
+                       "parallelism": f"dp{world}", "l2": "working set > L2 (no flush needed)",
+                       "bucket_mb": args.bucket_mb if world > 1 else None},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": int(x.nbytes + t.nbytes), "d2h_bytes_per_step": 4,
+                    "ms_per_step": e2e_ms / args.steps},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak,
+                         "unit": "TFLOP/s", "frac": achieved / tf32_peak if tf32_peak else None,
+                         "traffic": None,
+                         "kernel": "tc_gemm_kernel (3xTF32 tcgen05, all GEMM launches of the step)",
+                         "peak_note": f"{peak_src} bf16 dense {peaks['bf16_tflops']} TFLOP/s / 2 "
+                                      "(tf32 rate) / 3 (products per FP32 product)",
+                         "launches_per_step": tc_launches / args.steps},
+            "step_tflops": step_flops / (ms_step / 1e3) / 1e12,
+            "gpu_launches": int(launches),
+            "loss": loss_val,
+            "breakdown_ms": breakdown,
+            "clocks": clocks.summary(),
+        }
+        if cpu is not None:
+            result["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(result), flush=True)
+    if comm is not None:
+        tr.attach_comm(None)
+        comm.close()
+    tr.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--bucket-mb", type=int, default=64)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

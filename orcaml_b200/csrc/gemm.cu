@@ -1,0 +1,710 @@
+// gemm.cu -- GEMM kernels of the MLP step (see gemm.cuh for the operand format).
+//
+//  * tc_gemm_kernel: persistent warp-specialised tcgen05 kernel.  One CTA per
+//    SM; warp 0 issues TMA tile loads (hi and lo planes in one 3-D box), warp 1
+//    issues tcgen05.mma kind::tf32 (three products per k-step into one TMEM
+//    accumulator), warps 2-5 drain the double-buffered TMEM accumulator through
+//    the fused epilogue.  128x256 tiles, BK = 16, 4-stage smem ring.
+//  * simt_gemm_kernel: FFMA tiled kernel for shapes the tensor-core path does
+//    not take (tiny M/N, unaligned leading dimensions).
+//  * skinny kernels for the N <= 16 (logit layer, its dW) and K <= 16 (its dX)
+//    GEMMs of the classifier layer, which are memory-bound.
+//
+// The reference computes every product with `matrixmultiply::sgemm` in FP32
+// (orca-backend-cpu/src/backend.rs:130-221); all paths here are FP32-accurate:
+// SIMT kernels use fp32 FFMA on hi+lo (== x exactly), the tensor-core kernel
+// uses the 3xTF32 split with fp32 accumulation.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
+#include "gemm.cuh"
+
+namespace orca {
+
+// =============================================================== helpers
+__device__ __forceinline__ float ld_op(const float* hi, const float* lo, int64_t idx) {
+  float v = hi[idx];
+  if (lo) v = __fadd_rn(v, lo[idx]);
+  return v;
+}
+
+__device__ __forceinline__ void store_epi(const Epilogue& ep, int64_t m, int64_t n, float acc) {
+  const int64_t idx = m * ep.ldc + n;
+  switch (ep.mode) {
+    case EPI_STORE:
+      ep.out[idx] = acc;
+      break;
+    case EPI_BIAS:
+      ep.out[idx] = __fadd_rn(acc, ep.bias[n]);
+      break;
+    case EPI_BIAS_RELU_SPLIT: {
+      float y = __fadd_rn(acc, ep.bias[n]);
+      float a = y > 0.0f ? y : 0.0f;
+      float h, l;
+      split_tf32(a, h, l);
+      ep.out[idx] = h;
+      ep.out_lo[idx] = l;
+      break;
+    }
+    case EPI_MASK_SPLIT: {
+      float prev = __fadd_rn(ep.mask_hi[idx], ep.mask_lo[idx]);
+      float g = prev > 0.0f ? acc : 0.0f;
+      float h, l;
+      split_tf32(g, h, l);
+      ep.out[idx] = h;
+      ep.out_lo[idx] = l;
+      break;
+    }
+    case EPI_SPLIT: {
+      float h, l;
+      split_tf32(acc, h, l);
+      ep.out[idx] = h;
+      ep.out_lo[idx] = l;
+      break;
+    }
+  }
+}
+
+__global__ void split_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                             float* __restrict__ lo, int64_t n) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    float h, l;
+    split_tf32(x[i], h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+orca_status split_planes(orca_ctx* ctx, const float* x, float* hi, float* lo, int64_t n) {
+  if (n <= 0) return ORCA_OK;
+  int blocks = (int)std::min<int64_t>(cdiv(n, 256), (int64_t)ctx->sm_count * 8);
+  split_kernel<<<blocks, 256, 0, ctx->stream>>>(x, hi, lo, n);
+  count_launch(ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+// =============================================================== SIMT GEMM
+namespace simt {
+constexpr int BM = 64, BN = 64, BK = 16, THREADS = 256;
+
+__global__ void __launch_bounds__(THREADS)
+simt_gemm_kernel(int64_t M, int64_t N, int64_t K, Operand A, Operand B, Epilogue ep) {
+  __shared__ float As[BK][BM + 4];
+  __shared__ float Bs[BK][BN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < K; k0 += BK) {
+    // 64x16 A tile and 16x64 B tile, 1024 elements each: 4 per thread.
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      int e = tid + r * THREADS;
+      int mm, kk;
+      if (A.mn_major) { mm = e % BM; kk = e / BM; } else { kk = e % BK; mm = e / BK; }
+      int64_t gm = m0 + mm, gk = k0 + kk;
+      float v = 0.0f;
+      if (gm < M && gk < K) v = ld_op(A.hi, A.lo, A.mn_major ? gk * A.ld + gm : gm * A.ld + gk);
+      As[kk][mm] = v;
+      int nn;
+      if (B.mn_major) { nn = e % BN; kk = e / BN; } else { kk = e % BK; nn = e / BK; }
+      int64_t gn = n0 + nn;
+      gk = k0 + kk;
+      v = 0.0f;
+      if (gn < N && gk < K) v = ld_op(B.hi, B.lo, B.mn_major ? gk * B.ld + gn : gn * B.ld + gk);
+      Bs[kk][nn] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int64_t m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int64_t n = n0 + tx * 4 + j;
+      if (n < N) store_epi(ep, m, n, acc[i][j]);
+    }
+  }
+}
+}  // namespace simt
+
+// =============================================================== skinny kernels
+namespace skinny {
+constexpr int NMAX = 16;
+
+// N <= 16: one warp per output row; B staged through smem in K chunks.
+// A: any major; B: any major (read via ld_op).
+constexpr int KC = 512;
+__global__ void __launch_bounds__(256)
+narrow_n_kernel(int64_t M, int64_t N, int64_t K, Operand A, Operand B, Epilogue ep) {
+  __shared__ float Bs[KC][NMAX + 1];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t m = (int64_t)blockIdx.x * 8 + warp;
+  float acc[NMAX];
+#pragma unroll
+  for (int j = 0; j < NMAX; ++j) acc[j] = 0.0f;
+  for (int64_t k0 = 0; k0 < K; k0 += KC) {
+    const int kc = (int)std::min<int64_t>(KC, K - k0);
+    for (int e = threadIdx.x; e < KC * NMAX; e += blockDim.x) {
+      int kk = e / NMAX, nn = e % NMAX;
+      float v = 0.0f;
+      if (kk < kc && nn < N) {
+        int64_t gk = k0 + kk;
+        v = ld_op(B.hi, B.lo, B.mn_major ? gk * B.ld + nn : (int64_t)nn * B.ld + gk);
+      }
+      Bs[kk][nn] = v;
+    }
+    __syncthreads();
+    if (m < M) {
+      for (int kk = lane; kk < kc; kk += 32) {
+        int64_t gk = k0 + kk;
+        float a = ld_op(A.hi, A.lo, A.mn_major ? gk * A.ld + m : m * A.ld + gk);
+#pragma unroll
+        for (int j = 0; j < NMAX; ++j) acc[j] = fmaf(a, Bs[kk][j], acc[j]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < NMAX; ++j) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+  }
+  if (m < M && lane == 0) {
+    for (int j = 0; j < N; ++j) store_epi(ep, m, j, acc[j]);
+  }
+}
+
+// K <= 16: out[m, n] = sum_k A[m,k] B[k,n]; a block covers 32 rows x 256 cols.
+__global__ void __launch_bounds__(256)
+narrow_k_kernel(int64_t M, int64_t N, int64_t K, Operand A, Operand B, Epilogue ep) {
+  __shared__ float As[32][NMAX];
+  __shared__ float Bs[NMAX][256];
+  const int64_t m0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 256;
+  for (int e = threadIdx.x; e < 32 * NMAX; e += 256) {
+    int mm = e / NMAX, kk = e % NMAX;
+    int64_t gm = m0 + mm;
+    As[mm][kk] = (gm < M && kk < K)
+                     ? ld_op(A.hi, A.lo, A.mn_major ? (int64_t)kk * A.ld + gm : gm * A.ld + kk)
+                     : 0.0f;
+  }
+  for (int e = threadIdx.x; e < NMAX * 256; e += 256) {
+    int kk = e / 256, nn = e % 256;
+    int64_t gn = n0 + nn;
+    Bs[kk][nn] = (gn < N && kk < K)
+                     ? ld_op(B.hi, B.lo, B.mn_major ? (int64_t)kk * B.ld + gn : gn * B.ld + kk)
+                     : 0.0f;
+  }
+  __syncthreads();
+  const int64_t n = n0 + threadIdx.x;
+  if (n >= N) return;
+  for (int mm = 0; mm < 32; ++mm) {
+    const int64_t m = m0 + mm;
+    if (m >= M) break;
+    float acc = 0.0f;
+    for (int kk = 0; kk < K; ++kk) acc = fmaf(As[mm][kk], Bs[kk][threadIdx.x], acc);
+    store_epi(ep, m, n, acc);
+  }
+}
+
+// N <= 16 with a long K and a short M-parallel extent (dW of the classifier
+// layer: M = features, K = batch): thread per output row, split-K over blocks
+// into partials[split][M][N], reduced in split order by reduce_kernel.
+constexpr int SPLIT_KC = 256;
+__global__ void __launch_bounds__(256)
+narrow_n_splitk_kernel(int64_t M, int64_t N, int64_t K, Operand A, Operand B, float* partials,
+                       int64_t k_per_split) {
+  __shared__ float Bs[SPLIT_KC][NMAX];
+  const int64_t m = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  const int64_t kbeg = (int64_t)blockIdx.y * k_per_split;
+  const int64_t kend = std::min<int64_t>(K, kbeg + k_per_split);
+  float acc[NMAX];
+#pragma unroll
+  for (int j = 0; j < NMAX; ++j) acc[j] = 0.0f;
+  for (int64_t k0 = kbeg; k0 < kend; k0 += SPLIT_KC) {
+    const int kc = (int)std::min<int64_t>(SPLIT_KC, kend - k0);
+    for (int e = threadIdx.x; e < SPLIT_KC * NMAX; e += 256) {
+      int kk = e / NMAX, nn = e % NMAX;
+      float v = 0.0f;
+      if (kk < kc && nn < N) {
+        int64_t gk = k0 + kk;
+        v = ld_op(B.hi, B.lo, B.mn_major ? gk * B.ld + nn : (int64_t)nn * B.ld + gk);
+      }
+      Bs[kk][nn] = v;
+    }
+    __syncthreads();
+    if (m < M) {
+      for (int kk = 0; kk < kc; ++kk) {
+        int64_t gk = k0 + kk;
+        float a = ld_op(A.hi, A.lo, A.mn_major ? gk * A.ld + m : m * A.ld + gk);
+#pragma unroll
+        for (int j = 0; j < NMAX; ++j) acc[j] = fmaf(a, Bs[kk][j], acc[j]);
+      }
+    }
+    __syncthreads();
+  }
+  if (m < M) {
+    float* p = partials + ((int64_t)blockIdx.y * M + m) * NMAX;
+#pragma unroll
+    for (int j = 0; j < NMAX; ++j) p[j] = acc[j];
+  }
+}
+
+__global__ void reduce_kernel(int64_t M, int64_t N, int splits, const float* partials,
+                              Epilogue ep) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * N) return;
+  int64_t m = i / N, n = i % N;
+  float s = 0.0f;
+  for (int sp = 0; sp < splits; ++sp) s += partials[((int64_t)sp * M + m) * NMAX + n];
+  store_epi(ep, m, n, s);
+}
+}  // namespace skinny
+
+// =============================================================== tcgen05 GEMM
+namespace tc {
+constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int A_PLANE = BM * BK * 4;                 // 8 KB
+constexpr int B_PLANE = BN * BK * 4;                 // 16 KB
+constexpr int A_STAGE = 2 * A_PLANE;                 // hi + lo
+constexpr int B_STAGE = 2 * B_PLANE;
+constexpr int TILE_BYTES = STAGES * (A_STAGE + B_STAGE);   // 192 KB
+constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 2 * BN;                    // two accumulators
+constexpr int GROUP_M = 8;
+
+struct Params {
+  int64_t M, N, K;
+  int a_mn, b_mn;
+  Epilogue ep;
+  int* dev_err;
+};
+
+// UMMA shared-memory matrix descriptor (sm_100 layout: start>>4 [0,14),
+// LBO>>4 [16,30), SBO>>4 [32,46), version 1 at [46,48), swizzle mode [61,64)).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
+
+// Descriptor of one 8-deep k-step of one plane of a staged operand tile.
+//  K-major (box {16 k, rows, 2 planes}, 64B swizzle): row r at r*64 B, plane
+//    after rows*64 B; k-step ks starts 32 B further; 8-row groups 512 B apart.
+//  MN-major (boxes {32 mn, 16 k, 2 planes}, 128B swizzle, one per 32-wide mn
+//    chunk, 4 KB apart): k row at 128 B stride, lo plane 2 KB after hi; k-step
+//    ks = 8 k rows = 1 KB further.
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int rows, int plane,
+                                                 int ks) {
+  if (mn_major) {
+    uint32_t addr = base + plane * 2048 + ks * 1024;
+    return smem_desc(addr, 4096, 1024, LAYOUT_SW128);
+  }
+  uint32_t addr = base + plane * (rows * 64) + ks * 32;
+  return smem_desc(addr, 16, 512, LAYOUT_SW64);
+}
+
+__device__ __forceinline__ void tile_coords(int64_t tile, int64_t num_m, int64_t num_n,
+                                            int64_t& tm, int64_t& tn) {
+  const int64_t group_size = (int64_t)GROUP_M * num_n;
+  const int64_t group = tile / group_size;
+  const int64_t first_m = group * GROUP_M;
+  const int64_t gm = std::min<int64_t>(num_m - first_m, GROUP_M);
+  const int64_t r = tile % group_size;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+__device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
+                                             int mn_major, int rows, int64_t mn0, int64_t k0) {
+  if (mn_major) {
+    for (int c = 0; c < rows / 32; ++c)
+      tma_load_3d(dst + c * 4096, map, bar, (int)(mn0 + 32 * c), (int)k0, 0);
+  } else {
+    tma_load_3d(dst, map, bar, (int)k0, (int)mn0, 0);
+  }
+}
+
+__device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, int64_t N, int64_t m,
+                                               int64_t n0, const float (&v)[32]) {
+  if (m >= M) return;
+  const bool full = (n0 + 32 <= N) && ((ep.ldc & 3) == 0);
+  if (!full) {
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < N) store_epi(ep, m, n0 + j, v[j]);
+    return;
+  }
+  const int64_t base = m * ep.ldc + n0;
+  if (ep.mode == EPI_STORE || ep.mode == EPI_BIAS) {
+    float4* o = reinterpret_cast<float4*>(ep.out + base);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 r;
+      r.x = v[4 * q + 0]; r.y = v[4 * q + 1]; r.z = v[4 * q + 2]; r.w = v[4 * q + 3];
+      if (ep.mode == EPI_BIAS) {
+        r.x = __fadd_rn(r.x, ep.bias[n0 + 4 * q + 0]);
+        r.y = __fadd_rn(r.y, ep.bias[n0 + 4 * q + 1]);
+        r.z = __fadd_rn(r.z, ep.bias[n0 + 4 * q + 2]);
+        r.w = __fadd_rn(r.w, ep.bias[n0 + 4 * q + 3]);
+      }
+      o[q] = r;
+    }
+    return;
+  }
+  float4* oh = reinterpret_cast<float4*>(ep.out + base);
+  float4* ol = reinterpret_cast<float4*>(ep.out_lo + base);
+  const float4* mh = reinterpret_cast<const float4*>(ep.mask_hi + base);
+  const float4* ml = reinterpret_cast<const float4*>(ep.mask_lo + base);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float x[4] = {v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]};
+    if (ep.mode == EPI_BIAS_RELU_SPLIT) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float y = __fadd_rn(x[e], ep.bias[n0 + 4 * q + e]);
+        x[e] = y > 0.0f ? y : 0.0f;
+      }
+    } else if (ep.mode == EPI_MASK_SPLIT) {
+      float4 a = mh[q], b = ml[q];
+      x[0] = __fadd_rn(a.x, b.x) > 0.0f ? x[0] : 0.0f;
+      x[1] = __fadd_rn(a.y, b.y) > 0.0f ? x[1] : 0.0f;
+      x[2] = __fadd_rn(a.z, b.z) > 0.0f ? x[2] : 0.0f;
+      x[3] = __fadd_rn(a.w, b.w) > 0.0f ? x[3] : 0.0f;
+    }
+    float4 h, l;
+    split_tf32(x[0], h.x, l.x);
+    split_tf32(x[1], h.y, l.y);
+    split_tf32(x[2], h.z, l.z);
+    split_tf32(x[3], h.w, l.w);
+    oh[q] = h;
+    ol[q] = l;
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+               const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* a_tiles = smem;
+  uint8_t* b_tiles = smem + STAGES * A_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TILE_BYTES);
+  uint64_t* full_bar = bars;                 // [STAGES]
+  uint64_t* empty_bar = bars + STAGES;       // [STAGES]
+  uint64_t* tfull_bar = bars + 2 * STAGES;   // [2]
+  uint64_t* tempty_bar = bars + 2 * STAGES + 2;  // [2]
+  uint64_t* drain_bar = bars + 2 * STAGES + 4;   // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t num_m = cdiv(p.M, BM), num_n = cdiv(p.N, BN);
+  const int64_t num_tiles = num_m * num_n;
+  const int64_t nk = cdiv(p.K, BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = -1;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int64_t tm, tn;
+        tile_coords(tile, num_m, num_n, tm, tn);
+        for (int64_t kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.dev_err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_bar[stage], A_STAGE + B_STAGE);
+          load_operand(a_tiles + stage * A_STAGE, &map_a, &full_bar[stage], p.a_mn, BM, tm * BM,
+                       kb * BK);
+          load_operand(b_tiles + stage * B_STAGE, &map_b, &full_bar[stage], p.b_mn, BN, tn * BN,
+                       kb * BK);
+          issued[stage] = (int)phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Never leave with bulk copies in flight into this CTA's shared memory.
+      for (int s = 0; s < STAGES; ++s) {
+        if (issued[s] < 0) continue;
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(&full_bar[s], (uint32_t)issued[s]) &&
+               global_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)p.a_mn << 15) |
+                             ((uint32_t)p.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(BM >> 4) << 24);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t aphase = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty_bar[acc], aphase ^ 1u, abort_flag, p.dev_err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int64_t kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.dev_err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(a_tiles + stage * A_STAGE);
+          const uint32_t b_base = smem_u32(b_tiles + stage * B_STAGE);
+#pragma unroll
+          for (int ks = 0; ks < BK / 8; ++ks) {
+            const uint64_t a_hi = operand_desc(a_base, p.a_mn, BM, 0, ks);
+            const uint64_t a_lo = operand_desc(a_base, p.a_mn, BM, 1, ks);
+            const uint64_t b_hi = operand_desc(b_base, p.b_mn, BN, 0, ks);
+            const uint64_t b_lo = operand_desc(b_base, p.b_mn, BN, 1, ks);
+            const uint32_t first = (kb == 0 && ks == 0) ? 0u : 1u;
+            tc_mma_tf32(d_tmem, a_lo, b_hi, idesc, first);
+            tc_mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
+            tc_mma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
+          }
+          tc_commit(&empty_bar[stage]);   // frees the smem stage once these MMAs finish
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[acc]);       // accumulator ready for the epilogue
+        if (++acc == 2) { acc = 0; aphase ^= 1u; }
+      }
+      // Drain: every issued MMA has completed before TMEM is released.
+      tc_commit(drain_bar);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain_bar, 0) && global_ns() - t0 < kWaitLimitNs) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;              // TMEM lanes [32q, 32q+32)
+    int acc = 0;
+    uint32_t aphase = 0;
+    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int64_t tm, tn;
+      tile_coords(tile, num_m, num_n, tm, tn);
+      if (!mbar_wait(&tfull_bar[acc], aphase, abort_flag, p.dev_err)) break;
+      tc_fence_after();
+      const int64_t m = tm * BM + quarter * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        const uint32_t taddr =
+            tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32);
+        tmem_ld_32x32b_x32(taddr, v);
+        const int64_t n0 = tn * BN + c * 32;
+        if (n0 < p.N) epilogue_chunk(p.ep, p.M, p.N, m, n0, v);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) { acc = 0; aphase ^= 1u; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Tensor map over a plane pair [2][rows][ld] viewed as 3-D {inner, rows, 2}.
+static orca_status make_map(CUtensorMap* map, const Operand& op, int64_t inner_extent,
+                            int64_t outer_extent, int box_inner, int box_outer, bool mn_major) {
+  auto encode = get_encode_fn();
+  if (!encode) return fail(ORCA_CUDA_ERROR, "cuTensorMapEncodeTiled unavailable");
+  const int64_t plane_stride = (int64_t)(op.lo - op.hi);
+  cuuint64_t dims[3] = {(cuuint64_t)inner_extent, (cuuint64_t)outer_extent, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)(op.ld * 4), (cuuint64_t)(plane_stride * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(op.hi), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ORCA_CUDA_ERROR, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return ORCA_OK;
+}
+
+static bool operand_ok(const Operand& op) {
+  if (!op.hi || !op.lo) return false;
+  if (op.lo <= op.hi) return false;
+  if ((op.ld & 3) != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(op.hi) & 15) != 0) return false;
+  if ((((int64_t)(op.lo - op.hi)) & 3) != 0) return false;
+  return true;
+}
+
+bool eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const Operand& B,
+              const Epilogue& ep) {
+  if (M < 64 || N < 64 || K < BK) return false;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
+  if (!operand_ok(A) || !operand_ok(B)) return false;
+  (void)ep;
+  return true;
+}
+
+orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
+                   const Operand& B, const Epilogue& ep) {
+  static bool attr_set[64] = {};
+  if (ctx->device < 64 && !attr_set[ctx->device]) {
+    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES));
+    attr_set[ctx->device] = true;
+  }
+  CUtensorMap ma, mb;
+  // A: K-major rows = M (extent {K, M}); MN-major rows = K (extent {M, K}).
+  if (A.mn_major) ORCA_TRY(make_map(&ma, A, M, K, 32, BK, true));
+  else ORCA_TRY(make_map(&ma, A, K, M, BK, BM, false));
+  if (B.mn_major) ORCA_TRY(make_map(&mb, B, N, K, 32, BK, true));
+  else ORCA_TRY(make_map(&mb, B, K, N, BK, BN, false));
+  Params p;
+  p.M = M; p.N = N; p.K = K;
+  p.a_mn = A.mn_major ? 1 : 0;
+  p.b_mn = B.mn_major ? 1 : 0;
+  p.ep = ep;
+  p.dev_err = ctx->dev_err;
+  const int64_t tiles = cdiv(M, BM) * cdiv(N, BN);
+  const int grid = (int)std::min<int64_t>(tiles, ctx->sm_count);
+  tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
+  count_launch(ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+}  // namespace tc
+
+// =============================================================== dispatch
+int gemm_select(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
+                const Operand& B, const Epilogue& ep, int path) {
+  (void)ctx;
+  if (path == GEMM_SIMT) return GEMM_SIMT;
+  if (tc::eligible(M, N, K, A, B, ep)) return GEMM_TC;
+  return GEMM_SIMT;
+}
+
+orca_status gemm(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
+                 const Operand& B, const Epilogue& ep, int path, float* workspace,
+                 size_t workspace_bytes) {
+  if (M <= 0 || N <= 0) return ORCA_OK;
+  if (path == GEMM_TC && !tc::eligible(M, N, K, A, B, ep))
+    return fail(ORCA_INVALID_ARGUMENT, "gemm: shape/operands not eligible for the tcgen05 path");
+  if (path != GEMM_SIMT && K > 0 && tc::eligible(M, N, K, A, B, ep))
+    return tc::launch(ctx, M, N, K, A, B, ep);
+
+  if (N <= skinny::NMAX && K > 0) {
+    // K-major A: a warp per row reads its row contiguously.  MN-major A (the
+    // dW of the classifier layer): a thread per row, rows contiguous across
+    // the warp, K split over blocks.
+    if (!A.mn_major && (M >= 2048 || K < 4 * M)) {
+      const int64_t rows_blocks = cdiv(M, 8);
+      skinny::narrow_n_kernel<<<(unsigned)rows_blocks, 256, 0, ctx->stream>>>(M, N, K, A, B, ep);
+      count_launch(ctx);
+      ORCA_CUDA_TRY(cudaGetLastError());
+      return ORCA_OK;
+    }
+    // Long K, short M: split K across blocks (deterministic two-level sum).
+    int splits = (int)std::min<int64_t>(64, std::max<int64_t>(1, K / 512));
+    const int64_t m_blocks = cdiv(M, 256);
+    while (splits > 1 && m_blocks * splits > 4 * (int64_t)ctx->sm_count) splits /= 2;
+    const int64_t kps = cdiv(K, splits);
+    const size_t need = (size_t)splits * (size_t)M * skinny::NMAX * sizeof(float);
+    float* part = workspace;
+    bool owned = false;
+    if (!part || workspace_bytes < need) {
+      ORCA_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&part), need, ctx->stream));
+      owned = true;
+    }
+    dim3 grid((unsigned)m_blocks, (unsigned)splits);
+    skinny::narrow_n_splitk_kernel<<<grid, 256, 0, ctx->stream>>>(M, N, K, A, B, part, kps);
+    skinny::reduce_kernel<<<(unsigned)cdiv(M * N, 256), 256, 0, ctx->stream>>>(M, N, splits,
+                                                                                part, ep);
+    count_launch(ctx, 2);
+    cudaError_t e = cudaGetLastError();
+    if (owned) cudaFreeAsync(part, ctx->stream);
+    if (e != cudaSuccess) return fail(ORCA_CUDA_ERROR, "skinny split-K: %s", cudaGetErrorString(e));
+    return ORCA_OK;
+  }
+  if (K <= skinny::NMAX && K > 0) {
+    dim3 grid((unsigned)cdiv(N, 256), (unsigned)cdiv(M, 32));
+    skinny::narrow_k_kernel<<<grid, 256, 0, ctx->stream>>>(M, N, K, A, B, ep);
+    count_launch(ctx);
+    ORCA_CUDA_TRY(cudaGetLastError());
+    return ORCA_OK;
+  }
+  dim3 grid((unsigned)cdiv(N, simt::BN), (unsigned)cdiv(M, simt::BM));
+  if (grid.y > 65535) return fail(ORCA_INVALID_ARGUMENT, "gemm: M too large for the SIMT path");
+  simt::simt_gemm_kernel<<<grid, simt::THREADS, 0, ctx->stream>>>(M, N, K, A, B, ep);
+  count_launch(ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+}  // namespace orca

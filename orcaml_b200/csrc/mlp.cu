@@ -1,0 +1,958 @@
+// mlp.cu -- the data-parallel MLP training step on device-resident state.
+//
+// One step = python/orca/nn/model.py:546-552 (zero_grad, forward, loss,
+// backward, all_reduce_gradients, optimizer.step) for
+// Sequential(Linear, ReLU, ..., Linear) + CrossEntropyLoss + SGD/AdamW:
+//
+//   forward   Z = X @ W (+ b, ReLU) ........ tcgen05 GEMM, bias+ReLU+split epilogue
+//   loss      softmax-CE fwd+bwd ........... ce_kernel (one thread per row)
+//   backward  db = colsum(dZ) .............. colsum kernels
+//             dW = X^T @ dZ ................ GEMM, MN-major A and B (no transposes)
+//             dX = dZ @ W^T, * (X > 0) ..... GEMM, K-major B, ReLU-mask+split epilogue
+//   exchange  all-reduce average of each layer's (dW, db) on the comm stream,
+//             started as soon as that layer's gradients exist
+//   update    SGD / SGD-momentum / AdamW kernels with the reference's per-op
+//             f32 rounding, writing the weights back as (hi, lo) planes.
+//
+// GEMM operands live as (hi, lo) plane pairs (gemm.cuh); the reference's
+// [in, out] weight layout (python/orca/nn/linear.py:29) is kept.
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace orca {
+orca_status comm_allreduce_avg_stream(orca_comm* comm, float* ptr, size_t n, cudaStream_t stream);
+}  // namespace orca
+
+namespace orca {
+
+// ---------------------------------------------------------------- kernels
+// Softmax cross-entropy forward + backward for one row per thread, restating
+// python/orca/nn/loss.py:83-100 and the reverse sweep of the tape nodes it
+// records (orca-autograd/src/backend.rs; see oracle/orca_oracle.c
+// oc_softmax_ce for the node-by-node derivation).  row_loss[b] gets
+// sum_c -(t*ls); the mean is taken by ce_loss_kernel.
+__global__ void ce_kernel(const float* __restrict__ P, const float* __restrict__ T, int64_t B,
+                          int64_t C, float inv_b, float* __restrict__ dP,
+                          float* __restrict__ row_loss) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const float* p = P + b * C;
+  const float* t = T + b * C;
+  float m = -3.402823466e38f;
+  for (int64_t c = 0; c < C; ++c) m = p[c] > m ? p[c] : m;
+  float s = 0.0f;
+  for (int64_t c = 0; c < C; ++c) s = __fadd_rn(s, expf(__fsub_rn(p[c], m)));
+  const float lse = __fadd_rn(m, logf(fmaxf(s, 1e-7f)));
+  float per = 0.0f;
+  for (int64_t c = 0; c < C; ++c) {
+    const float ls = __fsub_rn(p[c], lse);
+    per = __fadd_rn(per, __fmul_rn(__fmul_rn(t[c], ls), -1.0f));
+  }
+  row_loss[b] = per;
+  if (!dP) return;
+  float* d = dP + b * C;
+  const float g_tl = __fmul_rn(inv_b, -1.0f);
+  float g_s0 = 0.0f;
+  for (int64_t c = 0; c < C; ++c) {
+    const float g_ls = __fadd_rn(0.0f, __fmul_rn(g_tl, t[c]));
+    const float g_lse = __fadd_rn(0.0f, __fmul_rn(g_ls, -1.0f));
+    g_s0 = __fadd_rn(g_s0, __fdiv_rn(__fadd_rn(0.0f, g_lse), s));
+  }
+  float g_m0 = 0.0f;
+  for (int64_t c = 0; c < C; ++c) {
+    const float g_ls = __fadd_rn(0.0f, __fmul_rn(g_tl, t[c]));
+    const float g_lse = __fadd_rn(0.0f, __fmul_rn(g_ls, -1.0f));
+    const float e = expf(__fsub_rn(p[c], m));
+    const float g_s = __fmul_rn(g_s0, e);
+    g_m0 = __fadd_rn(g_m0, __fadd_rn(__fadd_rn(0.0f, g_lse), __fadd_rn(0.0f, __fmul_rn(g_s, -1.0f))));
+    d[c] = __fadd_rn(__fadd_rn(0.0f, g_ls), __fadd_rn(0.0f, g_s));
+  }
+  for (int64_t c = 0; c < C; ++c) {
+    const float gi = p[c] == m ? __fadd_rn(0.0f, g_m0) : 0.0f;
+    d[c] = __fadd_rn(d[c], gi);
+  }
+}
+
+// loss = (sum_b row_loss[b]) * (1/B); a fixed-shape tree, so deterministic.
+__global__ void ce_loss_kernel(const float* __restrict__ row_loss, int64_t B, float inv_b,
+                               float* __restrict__ loss) {
+  __shared__ float sh[1024];
+  float acc = 0.0f;
+  for (int64_t i = threadIdx.x; i < B; i += blockDim.x) acc += row_loss[i];
+  sh[threadIdx.x] = acc;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) sh[threadIdx.x] += sh[threadIdx.x + s];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) loss[0] = __fmul_rn(sh[0], inv_b);
+}
+
+// db[n] = sum_b g[b, n]: partial sums over row chunks (grid.y), then an
+// ordered sum of the partials -- deterministic for a given shape.
+constexpr int COLSUM_ROWS = 256;
+__global__ void colsum_partial_kernel(const float* __restrict__ hi, const float* __restrict__ lo,
+                                      int64_t B, int64_t N, int64_t ld, float* __restrict__ part) {
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const int64_t b0 = (int64_t)blockIdx.y * COLSUM_ROWS;
+  const int64_t b1 = b0 + COLSUM_ROWS < B ? b0 + COLSUM_ROWS : B;
+  float acc = 0.0f;
+  for (int64_t b = b0; b < b1; ++b) {
+    float v = hi[b * ld + n];
+    if (lo) v = __fadd_rn(v, lo[b * ld + n]);
+    acc = __fadd_rn(acc, v);
+  }
+  part[(int64_t)blockIdx.y * N + n] = acc;
+}
+
+__global__ void colsum_final_kernel(const float* __restrict__ part, int chunks, int64_t N,
+                                    float* __restrict__ out) {
+  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float acc = 0.0f;
+  for (int c = 0; c < chunks; ++c) acc = __fadd_rn(acc, part[(int64_t)c * N + n]);
+  out[n] = acc;
+}
+
+struct SgdArgs {
+  float lr, wd, mom, one_minus_damp;
+  int use_wd, use_mom, use_damp, first;
+};
+
+// SGD.step (python/orca/optim/sgd.py:55-79), one rounding per reference op.
+// p is (hi, lo) planes when lo != nullptr, else plain fp32 in hi.
+__global__ void sgd_kernel(float* __restrict__ hi, float* __restrict__ lo,
+                           const float* __restrict__ g, float* __restrict__ v, int64_t n,
+                           SgdArgs a) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float p = lo ? __fadd_rn(hi[i], lo[i]) : hi[i];
+    float gi = g[i];
+    if (a.use_wd) gi = __fadd_rn(gi, __fmul_rn(p, a.wd));
+    if (a.use_mom) {
+      float vi;
+      if (a.first) vi = gi;
+      else if (a.use_damp) vi = __fadd_rn(__fmul_rn(v[i], a.mom), __fmul_rn(gi, a.one_minus_damp));
+      else vi = __fadd_rn(__fmul_rn(v[i], a.mom), gi);
+      v[i] = vi;
+      gi = vi;
+    }
+    p = __fsub_rn(p, __fmul_rn(gi, a.lr));
+    if (lo) {
+      float h, l;
+      split_tf32(p, h, l);
+      hi[i] = h;
+      lo[i] = l;
+    } else {
+      hi[i] = p;
+    }
+  }
+}
+
+struct AdamArgs {
+  float decay, b1, one_minus_b1, b2, one_minus_b2, bc1, bc2, eps, lr;
+};
+
+// AdamW.step (python/orca/optim/adamw.py:75-99), one rounding per reference op.
+__global__ void adamw_kernel(float* __restrict__ hi, float* __restrict__ lo,
+                             const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, int64_t n, AdamArgs a) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float p = lo ? __fadd_rn(hi[i], lo[i]) : hi[i];
+    const float gi = g[i];
+    const float decayed = __fmul_rn(p, a.decay);
+    const float mi = __fadd_rn(__fmul_rn(m[i], a.b1), __fmul_rn(gi, a.one_minus_b1));
+    const float vi = __fadd_rn(__fmul_rn(v[i], a.b2), __fmul_rn(__fmul_rn(gi, gi), a.one_minus_b2));
+    m[i] = mi;
+    v[i] = vi;
+    const float mh = __fmul_rn(mi, a.bc1);
+    const float vh = __fmul_rn(vi, a.bc2);
+    const float denom = __fadd_rn(__fsqrt_rn(vh), a.eps);
+    const float upd = __fmul_rn(__fdiv_rn(mh, denom), a.lr);
+    const float np = __fsub_rn(decayed, upd);
+    if (lo) {
+      float h, l;
+      split_tf32(np, h, l);
+      hi[i] = h;
+      lo[i] = l;
+    } else {
+      hi[i] = np;
+    }
+  }
+}
+
+__global__ void merge_planes_kernel(const float* __restrict__ hi, const float* __restrict__ lo,
+                                    float* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __fadd_rn(hi[i], lo[i]);
+}
+
+static SgdArgs sgd_args(double lr, double mom, double damp, double wd, int first) {
+  SgdArgs a;
+  a.lr = (float)lr;
+  a.wd = (float)wd;
+  a.mom = (float)mom;
+  a.one_minus_damp = (float)(1.0 - damp);
+  a.use_wd = wd != 0.0;
+  a.use_mom = mom != 0.0;
+  a.use_damp = damp != 0.0;
+  a.first = first;
+  return a;
+}
+
+static AdamArgs adam_args(double lr, double b1, double b2, double eps, double wd, int64_t t) {
+  AdamArgs a;
+  a.decay = (float)(1.0 - lr * wd);
+  a.b1 = (float)b1;
+  a.one_minus_b1 = (float)(1.0 - b1);
+  a.b2 = (float)b2;
+  a.one_minus_b2 = (float)(1.0 - b2);
+  a.bc1 = (float)(1.0 / (1.0 - std::pow(b1, (double)t)));
+  a.bc2 = (float)(1.0 / (1.0 - std::pow(b2, (double)t)));
+  a.eps = (float)eps;
+  a.lr = (float)lr;
+  return a;
+}
+
+static int ew_grid(orca_ctx* ctx, int64_t n) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), (int64_t)ctx->sm_count * 8));
+}
+
+orca_status colsum(orca_ctx* ctx, const float* hi, const float* lo, int64_t B, int64_t N,
+                   int64_t ld, float* out, float* part) {
+  const int chunks = (int)cdiv(B, COLSUM_ROWS);
+  dim3 g1((unsigned)cdiv(N, 256), (unsigned)chunks);
+  colsum_partial_kernel<<<g1, 256, 0, ctx->stream>>>(hi, lo, B, N, ld, part);
+  colsum_final_kernel<<<(unsigned)cdiv(N, 256), 256, 0, ctx->stream>>>(part, chunks, N, out);
+  count_launch(ctx, 2);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+}  // namespace orca
+
+using namespace orca;
+
+// =============================================================== step runner
+struct orca_mlp {
+  orca_ctx* ctx = nullptr;
+  int L = 0;
+  std::vector<int64_t> dims;
+  int64_t B = 0;
+  orca_optimizer opt = ORCA_OPT_SGD;
+  double lr = 0, mom = 0, damp = 0, wd = 0, b1 = 0.9, b2 = 0.999, eps = 1e-8;
+  int gemm_path = GEMM_AUTO;
+  int64_t t = 0;                     // AdamW step count
+  bool vel_init = false;             // SGD momentum buffers hold a value
+  // parameters
+  std::vector<float*> w_hi, w_lo, bias;   // w_lo = w_hi + K*N (one allocation per weight)
+  std::vector<int64_t> p_off;        // offset of each parameter in the gradient arena
+  int64_t n_params = 0;
+  float* grads = nullptr;            // gradient arena, Module.parameters() order
+  float* state0 = nullptr;           // SGD velocity / AdamW m (same layout as grads)
+  float* state1 = nullptr;           // AdamW v
+  // activations
+  float* x_planes = nullptr;         // [2][B][dims[0]]
+  std::vector<float*> act_planes;    // act_planes[l] = [2][B][dims[l]], l = 1..L-1
+  float* t_buf = nullptr;            // one-hot target [B][C]
+  float* x_stage = nullptr;          // raw input [B][dims[0]]
+  float* logits = nullptr;           // [B][C]
+  float* dlogits = nullptr;          // [B][C]
+  float* row_loss = nullptr;         // [B]
+  float* loss = nullptr;             // [1]
+  float* dz[2] = {nullptr, nullptr}; // ping-pong (hi, lo) planes of hidden-layer dZ
+  int64_t dz_plane = 0;              // elements per plane in dz buffers
+  float* colsum_part = nullptr;
+  float* workspace = nullptr;
+  size_t workspace_bytes = 0;
+  std::vector<void*> allocs;
+  // data parallel
+  orca_comm* comm = nullptr;
+  size_t bucket_bytes = 0;
+  cudaEvent_t ev_layer[64];
+  cudaEvent_t ev_comm_done = nullptr;
+  int last_launches = 0;
+  // Optional per-kernel-group timing: CUDA events recorded on the compute
+  // stream around each group of a step while profiling is on.
+  struct ProfSite { std::string name; double flops = 0, bytes = 0; double ms = 0; int count = 0;
+                    int gemm_path = -1; };
+  struct ProfRec { int site; cudaEvent_t a, b; };
+  bool profiling = false;
+  std::vector<ProfSite> sites;
+  std::vector<ProfRec> recs;
+  std::vector<cudaEvent_t> event_pool;
+};
+
+static cudaEvent_t pool_event(orca_mlp* m) {
+  if (!m->event_pool.empty()) {
+    cudaEvent_t e = m->event_pool.back();
+    m->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Opens a timed group; returns a record index (or -1 when not profiling).
+static int prof_open(orca_mlp* m, const std::string& name, double flops, double bytes,
+                     int gemm_path = -1) {
+  if (!m->profiling) return -1;
+  int site = -1;
+  for (size_t i = 0; i < m->sites.size(); ++i)
+    if (m->sites[i].name == name) { site = (int)i; break; }
+  if (site < 0) {
+    orca_mlp::ProfSite ps;
+    ps.name = name;
+    ps.flops = flops;
+    ps.bytes = bytes;
+    ps.gemm_path = gemm_path;
+    m->sites.push_back(ps);
+    site = (int)m->sites.size() - 1;
+  }
+  orca_mlp::ProfRec r;
+  r.site = site;
+  r.a = pool_event(m);
+  r.b = pool_event(m);
+  cudaEventRecord(r.a, m->ctx->stream);
+  m->recs.push_back(r);
+  return (int)m->recs.size() - 1;
+}
+
+static void prof_close(orca_mlp* m, int rec) {
+  if (rec < 0) return;
+  cudaEventRecord(m->recs[rec].b, m->ctx->stream);
+}
+
+static orca_status mlp_alloc(orca_mlp* m, void** p, size_t bytes) {
+  ORCA_CUDA_TRY(cudaMalloc(p, bytes));
+  m->allocs.push_back(*p);
+  return ORCA_OK;
+}
+
+static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad);
+static orca_status mlp_backward_impl(orca_mlp* m);
+static orca_status mlp_update_impl(orca_mlp* m);
+
+extern "C" {
+
+orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp** out) {
+  ORCA_TRY(check_ctx(ctx));
+  if (!cfg || !out || !cfg->dims) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (cfg->n_layers < 1 || cfg->n_layers > 60) return fail(ORCA_INVALID_ARGUMENT, "n_layers");
+  if (cfg->batch < 1) return fail(ORCA_INVALID_ARGUMENT, "batch must be positive");
+  for (int i = 0; i <= cfg->n_layers; ++i)
+    if (cfg->dims[i] < 1) return fail(ORCA_INVALID_ARGUMENT, "dims must be positive");
+  // Hyper-parameter validation as the reference's optimizers do
+  // (python/orca/optim/optimizer.py:6-66, sgd.py:40-44, adamw.py:31-34).
+  auto finite_nonneg = [](double v) { return std::isfinite(v) && v >= 0.0; };
+  if (!finite_nonneg(cfg->lr)) return fail(ORCA_INVALID_ARGUMENT, "lr must be non-negative");
+  if (cfg->optimizer == ORCA_OPT_SGD) {
+    if (!finite_nonneg(cfg->momentum) || !finite_nonneg(cfg->weight_decay) ||
+        !finite_nonneg(cfg->dampening) || cfg->dampening > 1.0)
+      return fail(ORCA_INVALID_ARGUMENT, "invalid SGD hyper-parameters");
+  } else if (cfg->optimizer == ORCA_OPT_ADAMW) {
+    if (!(cfg->beta1 >= 0.0 && cfg->beta1 < 1.0) || !(cfg->beta2 >= 0.0 && cfg->beta2 < 1.0) ||
+        !(std::isfinite(cfg->eps) && cfg->eps > 0.0) || !finite_nonneg(cfg->weight_decay))
+      return fail(ORCA_INVALID_ARGUMENT, "invalid AdamW hyper-parameters");
+  } else {
+    return fail(ORCA_INVALID_ARGUMENT, "unknown optimizer %d", (int)cfg->optimizer);
+  }
+  orca_mlp* m = new orca_mlp();
+  m->ctx = ctx;
+  m->L = cfg->n_layers;
+  m->dims.assign(cfg->dims, cfg->dims + cfg->n_layers + 1);
+  m->B = cfg->batch;
+  m->opt = cfg->optimizer;
+  m->lr = cfg->lr;
+  m->mom = cfg->momentum;
+  m->damp = cfg->dampening;
+  m->wd = cfg->weight_decay;
+  m->b1 = cfg->beta1;
+  m->b2 = cfg->beta2;
+  m->eps = cfg->eps;
+  m->gemm_path = cfg->gemm_path;
+  const int L = m->L;
+  const int64_t B = m->B, C = m->dims[L];
+  auto cleanup = [&](orca_status s) {
+    orca_mlp_destroy(m);
+    return s;
+  };
+  int64_t off = 0;
+  m->w_hi.resize(L);
+  m->w_lo.resize(L);
+  m->bias.resize(L);
+  for (int l = 0; l < L; ++l) {
+    const int64_t K = m->dims[l], N = m->dims[l + 1];
+    void* p;
+    orca_status s = mlp_alloc(m, &p, (size_t)(2 * K * N) * 4);
+    if (s != ORCA_OK) return cleanup(s);
+    m->w_hi[l] = (float*)p;
+    m->w_lo[l] = (float*)p + K * N;
+    s = mlp_alloc(m, &p, (size_t)N * 4);
+    if (s != ORCA_OK) return cleanup(s);
+    m->bias[l] = (float*)p;
+    m->p_off.push_back(off);
+    off += K * N;
+    m->p_off.push_back(off);
+    off += N;
+  }
+  m->n_params = off;
+  void* p;
+  const size_t pbytes = (size_t)off * 4;
+#define ALLOC(field, bytes)                               \
+  do {                                                    \
+    orca_status _s = mlp_alloc(m, &p, (bytes));           \
+    if (_s != ORCA_OK) return cleanup(_s);                \
+    m->field = (float*)p;                                 \
+  } while (0)
+  ALLOC(grads, pbytes);
+  if (m->opt == ORCA_OPT_ADAMW || m->mom != 0.0) ALLOC(state0, pbytes);
+  if (m->opt == ORCA_OPT_ADAMW) ALLOC(state1, pbytes);
+  if (m->state0) cudaMemset(m->state0, 0, pbytes);
+  if (m->state1) cudaMemset(m->state1, 0, pbytes);
+  ALLOC(x_planes, (size_t)(2 * B * m->dims[0]) * 4);
+  ALLOC(x_stage, (size_t)(B * m->dims[0]) * 4);
+  ALLOC(t_buf, (size_t)(B * C) * 4);
+  ALLOC(logits, (size_t)(B * C) * 4);
+  ALLOC(dlogits, (size_t)(B * C) * 4);
+  ALLOC(row_loss, (size_t)B * 4);
+  ALLOC(loss, 64);
+  m->act_planes.assign(L, nullptr);
+  int64_t maxh = 1;
+  for (int l = 1; l < L; ++l) {
+    ALLOC(act_planes[l], (size_t)(2 * B * m->dims[l]) * 4);
+    maxh = std::max(maxh, m->dims[l]);
+  }
+  m->dz_plane = B * maxh;
+  ALLOC(dz[0], (size_t)(2 * m->dz_plane) * 4);
+  ALLOC(dz[1], (size_t)(2 * m->dz_plane) * 4);
+  int64_t maxn = C;
+  for (int l = 0; l <= L; ++l) maxn = std::max(maxn, m->dims[l]);
+  ALLOC(colsum_part, (size_t)(cdiv(B, COLSUM_ROWS) * maxn) * 4);
+  m->workspace_bytes = (size_t)64 * (size_t)maxn * 16 * 4;
+  ALLOC(workspace, m->workspace_bytes);
+#undef ALLOC
+  for (int l = 0; l < 64; ++l) m->ev_layer[l] = nullptr;
+  for (int l = 0; l < L; ++l)
+    if (cudaEventCreateWithFlags(&m->ev_layer[l], cudaEventDisableTiming) != cudaSuccess)
+      return cleanup(fail(ORCA_CUDA_ERROR, "event creation failed"));
+  if (cudaEventCreateWithFlags(&m->ev_comm_done, cudaEventDisableTiming) != cudaSuccess)
+    return cleanup(fail(ORCA_CUDA_ERROR, "event creation failed"));
+  if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(ORCA_CUDA_ERROR, "init sync"));
+  *out = m;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_destroy(orca_mlp* m) {
+  if (!m) return ORCA_OK;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  cudaStreamSynchronize(m->ctx->comm_stream);
+  for (void* p : m->allocs) cudaFree(p);
+  for (int l = 0; l < 64; ++l)
+    if (m->ev_layer[l]) cudaEventDestroy(m->ev_layer[l]);
+  if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
+  for (auto& r : m->recs) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
+  for (auto e : m->event_pool) cudaEventDestroy(e);
+  delete m;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_num_params(const orca_mlp* m, int* count) {
+  if (!m || !count) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  *count = 2 * m->L;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_param_numel(const orca_mlp* m, int index, int64_t* numel) {
+  if (!m || !numel || index < 0 || index >= 2 * m->L)
+    return fail(ORCA_INVALID_ARGUMENT, "bad parameter index");
+  const int l = index / 2;
+  *numel = (index % 2 == 0) ? m->dims[l] * m->dims[l + 1] : m->dims[l + 1];
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_set_param(orca_mlp* m, int index, const float* host, int64_t numel) {
+  int64_t n;
+  ORCA_TRY(orca_mlp_param_numel(m, index, &n));
+  if (n != numel || !host) return fail(ORCA_SHAPE_MISMATCH, "set_param: %lld elements expected",
+                                       (long long)n);
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  const int l = index / 2;
+  if (index % 2 == 0) {
+    // Stage through the gradient arena slot of this parameter, then split.
+    ORCA_CUDA_TRY(cudaMemcpyAsync(m->grads + m->p_off[index], host, (size_t)n * 4,
+                                  cudaMemcpyHostToDevice, m->ctx->stream));
+    ORCA_TRY(split_planes(m->ctx, m->grads + m->p_off[index], m->w_hi[l], m->w_lo[l], n));
+  } else {
+    ORCA_CUDA_TRY(cudaMemcpyAsync(m->bias[l], host, (size_t)n * 4, cudaMemcpyHostToDevice,
+                                  m->ctx->stream));
+  }
+  ORCA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_get_param(orca_mlp* m, int index, float* host, int64_t numel) {
+  int64_t n;
+  ORCA_TRY(orca_mlp_param_numel(m, index, &n));
+  if (n != numel || !host) return fail(ORCA_SHAPE_MISMATCH, "get_param: %lld elements expected",
+                                       (long long)n);
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  const int l = index / 2;
+  if (index % 2 == 0) {
+    float* tmp = nullptr;
+    ORCA_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&tmp), (size_t)n * 4, m->ctx->stream));
+    merge_planes_kernel<<<ew_grid(m->ctx, n), 256, 0, m->ctx->stream>>>(m->w_hi[l], m->w_lo[l],
+                                                                        tmp, n);
+    count_launch(m->ctx);
+    ORCA_CUDA_TRY(cudaMemcpyAsync(host, tmp, (size_t)n * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+    cudaFreeAsync(tmp, m->ctx->stream);
+  } else {
+    ORCA_CUDA_TRY(cudaMemcpyAsync(host, m->bias[l], (size_t)n * 4, cudaMemcpyDeviceToHost,
+                                  m->ctx->stream));
+  }
+  ORCA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+  return check_device_error(m->ctx);
+}
+
+orca_status orca_mlp_get_grad(orca_mlp* m, int index, float* host, int64_t numel) {
+  int64_t n;
+  ORCA_TRY(orca_mlp_param_numel(m, index, &n));
+  if (n != numel || !host) return fail(ORCA_SHAPE_MISMATCH, "get_grad: size");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  ORCA_CUDA_TRY(cudaMemcpyAsync(host, m->grads + m->p_off[index], (size_t)n * 4,
+                                cudaMemcpyDeviceToHost, m->ctx->stream));
+  ORCA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+  return check_device_error(m->ctx);
+}
+
+orca_status orca_mlp_attach_comm(orca_mlp* m, orca_comm* comm, size_t bucket_bytes) {
+  if (!m) return fail(ORCA_INVALID_ARGUMENT, "null mlp");
+  m->comm = comm;
+  m->bucket_bytes = bucket_bytes;
+  return ORCA_OK;
+}
+
+static orca_status step_device_locked(orca_mlp* m, const float* x_dev, const float* t_dev,
+                                      float* loss_dev) {
+  orca_ctx* ctx = m->ctx;
+  const uint64_t l0 = ctx->launches.load();
+  const int64_t B = m->B, C = m->dims[m->L];
+  const int pr = prof_open(m, "split_input", 0.0, 12.0 * B * m->dims[0]);
+  ORCA_TRY(split_planes(ctx, x_dev, m->x_planes, m->x_planes + B * m->dims[0], B * m->dims[0]));
+  prof_close(m, pr);
+  if (t_dev != m->t_buf)
+    ORCA_CUDA_TRY(cudaMemcpyAsync(m->t_buf, t_dev, (size_t)(B * C) * 4, cudaMemcpyDeviceToDevice,
+                                  ctx->stream));
+  ORCA_TRY(mlp_forward_impl(m, true));
+  ORCA_TRY(mlp_backward_impl(m));
+  ORCA_TRY(mlp_update_impl(m));
+  if (loss_dev && loss_dev != m->loss)
+    ORCA_CUDA_TRY(cudaMemcpyAsync(loss_dev, m->loss, 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  m->last_launches = (int)(ctx->launches.load() - l0);
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_step_device(orca_mlp* m, const float* x_dev, const float* t_dev,
+                                 float* loss_dev) {
+  if (!m || !x_dev || !t_dev) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  return step_device_locked(m, x_dev, t_dev, loss_dev);
+}
+
+orca_status orca_mlp_step(orca_mlp* m, const float* x, const float* t, float* loss) {
+  if (!m || !x || !t) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  orca_ctx* ctx = m->ctx;
+  const int64_t B = m->B, C = m->dims[m->L];
+  ORCA_CUDA_TRY(cudaMemcpyAsync(m->x_stage, x, (size_t)(B * m->dims[0]) * 4,
+                                cudaMemcpyHostToDevice, ctx->stream));
+  ORCA_CUDA_TRY(cudaMemcpyAsync(m->t_buf, t, (size_t)(B * C) * 4, cudaMemcpyHostToDevice,
+                                ctx->stream));
+  ORCA_TRY(step_device_locked(m, m->x_stage, m->t_buf, nullptr));
+  if (loss) {
+    ORCA_CUDA_TRY(cudaMemcpyAsync(loss, m->loss, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    return check_device_error(ctx);
+  }
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_forward(orca_mlp* m, const float* x, const float* t, float* logits,
+                             float* loss) {
+  if (!m || !x) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  orca_ctx* ctx = m->ctx;
+  const int64_t B = m->B, C = m->dims[m->L];
+  ORCA_CUDA_TRY(cudaMemcpyAsync(m->x_stage, x, (size_t)(B * m->dims[0]) * 4,
+                                cudaMemcpyHostToDevice, ctx->stream));
+  ORCA_TRY(split_planes(ctx, m->x_stage, m->x_planes, m->x_planes + B * m->dims[0],
+                        B * m->dims[0]));
+  if (t) {
+    ORCA_CUDA_TRY(cudaMemcpyAsync(m->t_buf, t, (size_t)(B * C) * 4, cudaMemcpyHostToDevice,
+                                  ctx->stream));
+  }
+  ORCA_TRY(mlp_forward_impl(m, false));
+  if (t) {
+    ce_kernel<<<(unsigned)cdiv(B, 128), 128, 0, ctx->stream>>>(m->logits, m->t_buf, B, C,
+                                                              1.0f / (float)B, nullptr,
+                                                              m->row_loss);
+    ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(m->row_loss, B, 1.0f / (float)B, m->loss);
+    count_launch(ctx, 2);
+  }
+  if (logits)
+    ORCA_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)(B * C) * 4, cudaMemcpyDeviceToHost,
+                                  ctx->stream));
+  if (loss && t)
+    ORCA_CUDA_TRY(cudaMemcpyAsync(loss, m->loss, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return check_device_error(ctx);
+}
+
+orca_status orca_mlp_profile_begin(orca_mlp* m) {
+  if (!m) return fail(ORCA_INVALID_ARGUMENT, "null mlp");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  m->profiling = true;
+  for (auto& s : m->sites) { s.ms = 0; s.count = 0; }
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_profile_end(orca_mlp* m, int* n_sites) {
+  if (!m || !n_sites) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  m->profiling = false;
+  ORCA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+  for (auto& r : m->recs) {
+    float ms = 0;
+    if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+      m->sites[r.site].ms += ms;
+      m->sites[r.site].count += 1;
+    }
+    m->event_pool.push_back(r.a);
+    m->event_pool.push_back(r.b);
+  }
+  m->recs.clear();
+  *n_sites = (int)m->sites.size();
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_profile_site(const orca_mlp* m, int i, const char** name, double* ms_total,
+                                  int* launches, double* flops_per_launch,
+                                  double* bytes_per_launch, int* gemm_path) {
+  if (!m || i < 0 || i >= (int)m->sites.size()) return fail(ORCA_INVALID_ARGUMENT, "bad site");
+  const auto& s = m->sites[i];
+  if (name) *name = s.name.c_str();
+  if (ms_total) *ms_total = s.ms;
+  if (launches) *launches = s.count;
+  if (flops_per_launch) *flops_per_launch = s.flops;
+  if (bytes_per_launch) *bytes_per_launch = s.bytes;
+  if (gemm_path) *gemm_path = s.gemm_path;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_launches_per_step(const orca_mlp* m, int* count) {
+  if (!m || !count) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  *count = m->last_launches;
+  return ORCA_OK;
+}
+
+}  // extern "C"
+
+// Forward: activations as planes; logits plain.  with_loss_grad also runs the
+// fused CE forward+backward into loss / dlogits.
+static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad) {
+  orca_ctx* ctx = m->ctx;
+  const int L = m->L;
+  const int64_t B = m->B, C = m->dims[L];
+  for (int l = 0; l < L; ++l) {
+    const int64_t K = m->dims[l], N = m->dims[l + 1];
+    Operand a, w;
+    a.hi = l == 0 ? m->x_planes : m->act_planes[l];
+    a.lo = a.hi + B * K;
+    a.ld = K;
+    a.mn_major = false;
+    w.hi = m->w_hi[l];
+    w.lo = m->w_lo[l];
+    w.ld = N;
+    w.mn_major = true;
+    Epilogue ep;
+    ep.bias = m->bias[l];
+    if (l + 1 < L) {
+      ep.mode = EPI_BIAS_RELU_SPLIT;
+      ep.out = m->act_planes[l + 1];
+      ep.out_lo = ep.out + B * N;
+      ep.ldc = N;
+    } else {
+      ep.mode = EPI_BIAS;
+      ep.out = m->logits;
+      ep.ldc = N;
+    }
+    const int path = gemm_select(ctx, B, N, K, a, w, ep, m->gemm_path);
+    const int pr = prof_open(m, "gemm_fwd_l" + std::to_string(l), 2.0 * B * N * K,
+                             4.0 * (2 * B * K + 2 * K * N + (l + 1 < L ? 2 : 1) * B * N), path);
+    ORCA_TRY(gemm(ctx, B, N, K, a, w, ep, m->gemm_path, m->workspace, m->workspace_bytes));
+    prof_close(m, pr);
+  }
+  if (with_loss_grad) {
+    const int pr = prof_open(m, "softmax_ce", 0.0, 4.0 * (3 * B * C + B));
+    ce_kernel<<<(unsigned)cdiv(B, 128), 128, 0, ctx->stream>>>(m->logits, m->t_buf, B, C,
+                                                              1.0f / (float)B, m->dlogits,
+                                                              m->row_loss);
+    ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(m->row_loss, B, 1.0f / (float)B, m->loss);
+    count_launch(ctx, 2);
+    prof_close(m, pr);
+    ORCA_CUDA_TRY(cudaGetLastError());
+  }
+  return ORCA_OK;
+}
+
+static orca_status launch_layer_allreduce(orca_mlp* m, int l) {
+  orca_ctx* ctx = m->ctx;
+  ORCA_CUDA_TRY(cudaEventRecord(m->ev_layer[l], ctx->stream));
+  ORCA_CUDA_TRY(cudaStreamWaitEvent(ctx->comm_stream, m->ev_layer[l], 0));
+  // The layer's (dW, db) are contiguous in the arena.
+  float* base = m->grads + m->p_off[2 * l];
+  size_t n = (size_t)(m->dims[l] * m->dims[l + 1] + m->dims[l + 1]);
+  size_t chunk = m->bucket_bytes ? std::max<size_t>(m->bucket_bytes / 4, 1) : n;
+  for (size_t off = 0; off < n; off += chunk) {
+    size_t c = std::min(chunk, n - off);
+    ORCA_TRY(comm_allreduce_avg_stream(m->comm, base + off, c, ctx->comm_stream));
+  }
+  return ORCA_OK;
+}
+
+static orca_status mlp_backward_impl(orca_mlp* m) {
+  orca_ctx* ctx = m->ctx;
+  const int L = m->L;
+  const int64_t B = m->B;
+  // g: gradient w.r.t. the current layer's pre-activation output.
+  const float* g_hi = m->dlogits;
+  const float* g_lo = nullptr;
+  int64_t g_ld = m->dims[L];
+  int cur = 0;
+  for (int l = L - 1; l >= 0; --l) {
+    const int64_t K = m->dims[l], N = m->dims[l + 1];
+    // db = sum over the batch (ExpandBackward -> sum_to_shape [B,N] -> [1,N]).
+    int pr = prof_open(m, "colsum_l" + std::to_string(l), (double)B * N,
+                       4.0 * ((g_lo ? 2 : 1) * B * N + N));
+    ORCA_TRY(colsum(ctx, g_hi, g_lo, B, N, g_ld, m->grads + m->p_off[2 * l + 1], m->colsum_part));
+    prof_close(m, pr);
+    // dW = act^T @ g : M = K (features), N, K_gemm = B.
+    Operand at, g;
+    at.hi = l == 0 ? m->x_planes : m->act_planes[l];
+    at.lo = at.hi + B * K;
+    at.ld = K;
+    at.mn_major = true;
+    g.hi = g_hi;
+    g.lo = g_lo;
+    g.ld = g_ld;
+    g.mn_major = true;
+    Epilogue ew;
+    ew.mode = EPI_STORE;
+    ew.out = m->grads + m->p_off[2 * l];
+    ew.ldc = N;
+    pr = prof_open(m, "gemm_dw_l" + std::to_string(l), 2.0 * B * N * K,
+                   4.0 * (2 * B * K + (g_lo ? 2 : 1) * B * N + K * N),
+                   gemm_select(ctx, K, N, B, at, g, ew, m->gemm_path));
+    ORCA_TRY(gemm(ctx, K, N, B, at, g, ew, m->gemm_path, m->workspace, m->workspace_bytes));
+    prof_close(m, pr);
+    if (m->comm) ORCA_TRY(launch_layer_allreduce(m, l));
+    if (l == 0) break;
+    // dX = g @ W^T, masked by the ReLU of the layer input (> 0), split.
+    Operand ga, wt;
+    ga.hi = g_hi;
+    ga.lo = g_lo;
+    ga.ld = g_ld;
+    ga.mn_major = false;
+    wt.hi = m->w_hi[l];
+    wt.lo = m->w_lo[l];
+    wt.ld = N;
+    wt.mn_major = false;
+    Epilogue ex;
+    ex.mode = EPI_MASK_SPLIT;
+    ex.out = m->dz[cur];
+    ex.out_lo = m->dz[cur] + B * K;
+    ex.ldc = K;
+    ex.mask_hi = m->act_planes[l];
+    ex.mask_lo = m->act_planes[l] + B * K;
+    pr = prof_open(m, "gemm_dx_l" + std::to_string(l), 2.0 * B * N * K,
+                   4.0 * ((g_lo ? 2 : 1) * B * N + 2 * K * N + 4 * B * K),
+                   gemm_select(ctx, B, K, N, ga, wt, ex, m->gemm_path));
+    ORCA_TRY(gemm(ctx, B, K, N, ga, wt, ex, m->gemm_path, m->workspace, m->workspace_bytes));
+    prof_close(m, pr);
+    g_hi = ex.out;
+    g_lo = ex.out_lo;
+    g_ld = K;
+    cur ^= 1;
+  }
+  if (m->comm) {
+    ORCA_CUDA_TRY(cudaEventRecord(m->ev_comm_done, ctx->comm_stream));
+    ORCA_CUDA_TRY(cudaStreamWaitEvent(ctx->stream, m->ev_comm_done, 0));
+  }
+  return ORCA_OK;
+}
+
+static orca_status mlp_update_impl(orca_mlp* m) {
+  orca_ctx* ctx = m->ctx;
+  const int L = m->L;
+  if (m->opt == ORCA_OPT_ADAMW) m->t += 1;
+  // Algorithmic bytes per parameter: SGD reads p, g and writes p (12 B);
+  // momentum adds v read + write (20 B); AdamW reads p, g, m, v, writes p, m, v (28 B).
+  const double bpp = m->opt == ORCA_OPT_ADAMW ? 28.0 : (m->mom != 0.0 ? 20.0 : 12.0);
+  const int pr = prof_open(m, "optimizer", 0.0, bpp * (double)m->n_params);
+  for (int l = 0; l < L; ++l) {
+    const int64_t K = m->dims[l], N = m->dims[l + 1];
+    for (int which = 0; which < 2; ++which) {
+      const int idx = 2 * l + which;
+      const int64_t n = which == 0 ? K * N : N;
+      float* hi = which == 0 ? m->w_hi[l] : m->bias[l];
+      float* lo = which == 0 ? m->w_lo[l] : nullptr;
+      const float* g = m->grads + m->p_off[idx];
+      if (m->opt == ORCA_OPT_SGD) {
+        float* v = m->state0 ? m->state0 + m->p_off[idx] : nullptr;
+        SgdArgs a = sgd_args(m->lr, m->mom, m->damp, m->wd, m->vel_init ? 0 : 1);
+        sgd_kernel<<<ew_grid(ctx, n), 256, 0, ctx->stream>>>(hi, lo, g, v, n, a);
+      } else {
+        AdamArgs a = adam_args(m->lr, m->b1, m->b2, m->eps, m->wd, m->t);
+        adamw_kernel<<<ew_grid(ctx, n), 256, 0, ctx->stream>>>(
+            hi, lo, g, m->state0 + m->p_off[idx], m->state1 + m->p_off[idx], n, a);
+      }
+      count_launch(ctx);
+    }
+  }
+  prof_close(m, pr);
+  m->vel_init = true;
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+// =============================================================== fused ops on buffers
+extern "C" {
+
+orca_status orca_linear_fwd(orca_ctx* ctx, const orca_buf* x, const orca_buf* w, const orca_buf* b,
+                            int64_t m, int64_t k, int64_t n, int relu, orca_buf** out) {
+  ORCA_TRY(check_ctx(ctx));
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (!x || !w || !out) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (x->n < (size_t)(m * k) || w->n < (size_t)(k * n) || (b && b->n < (size_t)n))
+    return fail(ORCA_SHAPE_MISMATCH, "linear_fwd: buffer sizes");
+  ORCA_TRY(new_buf(ctx, (size_t)(m * n), ORCA_F32, out));
+  float* scratch = nullptr;
+  const size_t elems = 2 * (size_t)(m * k) + 2 * (size_t)(k * n) + (relu ? 2 * (size_t)(m * n) : 0) +
+                       (b ? 0 : (size_t)n);
+  ORCA_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&scratch), elems * 4, ctx->stream));
+  float* xh = scratch;
+  float* wh = xh + 2 * m * k;
+  float* oh = wh + 2 * k * n;
+  float* zb = relu ? oh + 2 * m * n : oh;
+  ORCA_TRY(split_planes(ctx, (const float*)x->ptr, xh, xh + m * k, m * k));
+  ORCA_TRY(split_planes(ctx, (const float*)w->ptr, wh, wh + k * n, k * n));
+  const float* bias = (const float*)(b ? b->ptr : nullptr);
+  if (!b) {
+    ORCA_CUDA_TRY(cudaMemsetAsync(zb, 0, (size_t)n * 4, ctx->stream));
+    bias = zb;
+  }
+  Operand oa, ob;
+  oa.hi = xh; oa.lo = xh + m * k; oa.ld = k;
+  ob.hi = wh; ob.lo = wh + k * n; ob.ld = n; ob.mn_major = true;
+  Epilogue ep;
+  ep.bias = bias;
+  ep.ldc = n;
+  if (relu) {
+    ep.mode = EPI_BIAS_RELU_SPLIT;
+    ep.out = oh;
+    ep.out_lo = oh + m * n;
+  } else {
+    ep.mode = EPI_BIAS;
+    ep.out = (float*)(*out)->ptr;
+  }
+  orca_status s = gemm(ctx, m, n, k, oa, ob, ep, GEMM_AUTO);
+  if (s == ORCA_OK && relu) {
+    merge_planes_kernel<<<ew_grid(ctx, m * n), 256, 0, ctx->stream>>>(oh, oh + m * n,
+                                                                      (float*)(*out)->ptr, m * n);
+    count_launch(ctx);
+  }
+  cudaFreeAsync(scratch, ctx->stream);
+  return s;
+}
+
+orca_status orca_softmax_ce_fwd_bwd(orca_ctx* ctx, const orca_buf* logits, const orca_buf* target,
+                                    int64_t batch, int64_t classes, orca_buf** loss,
+                                    orca_buf** dlogits) {
+  ORCA_TRY(check_ctx(ctx));
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (!logits || !target || !loss) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (batch < 1 || classes < 1) return fail(ORCA_INVALID_ARGUMENT, "empty batch");
+  if (logits->n < (size_t)(batch * classes) || target->n < (size_t)(batch * classes))
+    return fail(ORCA_SHAPE_MISMATCH, "softmax_ce: buffer sizes");
+  ORCA_TRY(new_buf(ctx, 1, ORCA_F32, loss));
+  float* dp = nullptr;
+  if (dlogits) {
+    ORCA_TRY(new_buf(ctx, (size_t)(batch * classes), ORCA_F32, dlogits));
+    dp = (float*)(*dlogits)->ptr;
+  }
+  float* rows = nullptr;
+  ORCA_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&rows), (size_t)batch * 4, ctx->stream));
+  const float inv_b = 1.0f / (float)batch;
+  ce_kernel<<<(unsigned)cdiv(batch, 128), 128, 0, ctx->stream>>>(
+      (const float*)logits->ptr, (const float*)target->ptr, batch, classes, inv_b, dp, rows);
+  ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(rows, batch, inv_b, (float*)(*loss)->ptr);
+  count_launch(ctx, 2);
+  cudaFreeAsync(rows, ctx->stream);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+orca_status orca_sgd_step(orca_ctx* ctx, orca_buf* p, const orca_buf* g, orca_buf* v, double lr,
+                          double momentum, double dampening, double weight_decay, int first) {
+  ORCA_TRY(check_ctx(ctx));
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (!p || !g) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (g->n != p->n || (v && v->n != p->n)) return fail(ORCA_SHAPE_MISMATCH, "sgd_step: sizes");
+  if (momentum != 0.0 && !v) return fail(ORCA_INVALID_ARGUMENT, "sgd_step: momentum needs v");
+  const int64_t n = (int64_t)p->n;
+  SgdArgs a = sgd_args(lr, momentum, dampening, weight_decay, first);
+  sgd_kernel<<<ew_grid(ctx, n), 256, 0, ctx->stream>>>((float*)p->ptr, nullptr,
+                                                       (const float*)g->ptr,
+                                                       v ? (float*)v->ptr : nullptr, n, a);
+  count_launch(ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+orca_status orca_adamw_step(orca_ctx* ctx, orca_buf* p, const orca_buf* g, orca_buf* m,
+                            orca_buf* v, double lr, double beta1, double beta2, double eps,
+                            double weight_decay, int64_t t) {
+  ORCA_TRY(check_ctx(ctx));
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (!p || !g || !m || !v) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (g->n != p->n || m->n != p->n || v->n != p->n)
+    return fail(ORCA_SHAPE_MISMATCH, "adamw_step: sizes");
+  if (t < 1) return fail(ORCA_INVALID_ARGUMENT, "adamw_step: t starts at 1");
+  const int64_t n = (int64_t)p->n;
+  AdamArgs a = adam_args(lr, beta1, beta2, eps, weight_decay, t);
+  adamw_kernel<<<ew_grid(ctx, n), 256, 0, ctx->stream>>>((float*)p->ptr, nullptr,
+                                                         (const float*)g->ptr, (float*)m->ptr,
+                                                         (float*)v->ptr, n, a);
+  count_launch(ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,100 @@
+"""FP32-accuracy of the GEMM paths, through orca_gemm_ex / orca_matmul / orca_linear_fwd.
+
+Every operand orientation the MLP step uses (X@W: A K-major, B MN-major;
+X^T@dY: both MN-major; dY@W^T: both K-major) is checked on the tcgen05
+3xTF32 path and on the SIMT path against a float64 product, including
+ragged M/N/K tails (K = 784, N = 1000, M = 100) that exercise TMA
+out-of-bounds fill and the epilogue's edge masks.
+"""
+import numpy as np
+import pytest
+
+from tests.gpu_util import assert_fp32_gemm
+
+pytestmark = pytest.mark.gpu
+
+RNG = np.random.default_rng(3)
+
+
+@pytest.fixture(scope="module")
+def be():
+    from orcaml_b200.backend import CudaBackend
+    b = CudaBackend(0)
+    yield b
+    b.close()
+
+
+def run(be, m, n, k, a_mn, b_mn, path, scale=1.0):
+    a = (RNG.standard_normal((k, m) if a_mn else (m, k)) * scale).astype(np.float32)
+    b = (RNG.standard_normal((k, n) if b_mn else (n, k)) * scale).astype(np.float32)
+    sa = be.from_f32_slice([a.size], a)
+    sb = be.from_f32_slice([b.size], b)
+    c = be.to_f32_vec(be.gemm_ex(m, n, k, sa, a_mn, sb, b_mn, path)).reshape(m, n)
+    A = a.T if a_mn else a
+    B = b if b_mn else b.T
+    return c, A, B
+
+
+SHAPES = [(128, 256, 16), (256, 512, 64), (384, 768, 784), (100, 1000, 200), (1000, 300, 48),
+          (520, 260, 4096)]
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (False, False), (True, False)])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_tcgen05_orientations(be, m, n, k, a_mn, b_mn):
+    c, A, B = run(be, m, n, k, a_mn, b_mn, path=2)
+    assert_fp32_gemm(c, A, B)
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (False, False)])
+@pytest.mark.parametrize("m,n,k", [(37, 53, 29), (4096, 10, 512), (64, 10, 4096), (300, 200, 10),
+                                   (128, 128, 128)])
+def test_simt_and_skinny(be, m, n, k, a_mn, b_mn):
+    c, A, B = run(be, m, n, k, a_mn, b_mn, path=1)
+    assert_fp32_gemm(c, A, B)
+
+
+def test_tcgen05_is_not_plain_tf32(be):
+    """A TF32-only product misses the bound by ~3 orders of magnitude; the
+    split path meets it -- evidence that the lo planes are being used."""
+    c, A, B = run(be, 256, 256, 1024, False, True, path=2)
+    assert_fp32_gemm(c, A, B, tol=2e-6)
+    t32 = lambda x: (x.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    c_tf32 = (t32(A).astype(np.float64) @ t32(B).astype(np.float64)).astype(np.float32)
+    with pytest.raises(AssertionError):
+        assert_fp32_gemm(c_tf32, A, B, tol=2e-6)
+
+
+def test_tcgen05_large_tiles_and_waves(be):
+    # More tiles than SMs (persistent scheduler wraps), both accumulators reused.
+    c, A, B = run(be, 2048, 4096, 256, False, True, path=2)
+    assert_fp32_gemm(c, A, B)
+
+
+def test_path_rejects_ineligible(be):
+    from orcaml_b200._lib import OrcaError
+    with pytest.raises(OrcaError):
+        run(be, 32, 32, 8, False, True, path=2)   # too small for the tensor-core tile
+
+
+def test_matmul_trait_method_batched(be):
+    a = RNG.standard_normal((3, 130, 96)).astype(np.float32)
+    b = RNG.standard_normal((3, 96, 200)).astype(np.float32)
+    c = be.to_f32_vec(be.matmul(be.from_f32_slice([3, 130, 96], a),
+                                be.from_f32_slice([3, 96, 200], b),
+                                [3, 130, 96], [3, 96, 200])).reshape(3, 130, 200)
+    for i in range(3):
+        assert_fp32_gemm(c[i], a[i], b[i])
+
+
+def test_linear_fwd_bias_relu(be):
+    m, k, n = 300, 784, 512
+    x = RNG.random((m, k), dtype=np.float32)
+    w = (RNG.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    bias = (RNG.uniform(-1, 1, (1, n)) / np.sqrt(k)).astype(np.float32)
+    out = be.to_f32_vec(be.linear_fwd(be.from_f32_slice([m, k], x), be.from_f32_slice([k, n], w),
+                                      be.from_f32_slice([1, n], bias), m, k, n, relu=True))
+    z = x.astype(np.float64) @ w.astype(np.float64) + bias
+    ref = np.maximum(z, 0)
+    scale = np.abs(x).astype(np.float64) @ np.abs(w).astype(np.float64) + np.abs(bias)
+    assert np.all(np.abs(out.reshape(m, n) - ref) <= 2e-6 * scale + 1e-30)

@@ -1,0 +1,157 @@
+"""The fused training step on the GPU vs the oracle (the reference's own
+composition, pinned by the golden fixtures), through the C ABI.
+
+Bar (north star): per-step loss and final parameters within 1e-4 relative
+after 20 steps, identical argmax predictions.  The tolerance covers the
+unpinned summation order of the reference's GEMM (`matrixmultiply`); all
+non-GEMM arithmetic follows the reference op by op.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from orcaml_b200.synthetic import CONFIGS, init_params, make_batch
+from tests.gpu_util import rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+
+
+@pytest.fixture(scope="module")
+def be():
+    from orcaml_b200.backend import CudaBackend
+    b = CudaBackend(0)
+    yield b
+    b.close()
+
+
+def make(be, dims, batch, opt, gemm_path="auto", **kw):
+    from orcaml_b200.mlp import MlpTrainer
+    tr = MlpTrainer(be, dims, batch, optimizer=opt, gemm_path=gemm_path, **kw)
+    tr.set_parameters(init_params(dims, 1))
+    return tr
+
+
+def oracle_trainer(dims, opt, **kw):
+    return O.OracleTrainer(dims, init_params(dims, 1), optimizer=opt, **kw)
+
+
+@pytest.mark.parametrize("gemm_path", ["auto", "simt"])
+def test_c0_twenty_steps_match_oracle(be, gemm_path):
+    """784-512-512-10, B=128, SGD lr 0.1, 20 steps."""
+    cfg = CONFIGS["c0"]
+    x, t, _ = make_batch(cfg.dims, cfg.batch, 0)
+    tr = make(be, cfg.dims, cfg.batch, "sgd", gemm_path, lr=cfg.lr)
+    ref = oracle_trainer(cfg.dims, "sgd", lr=cfg.lr)
+    for step in range(20):
+        lg = tr.step(x, t)
+        lr_ = ref.step(x, t)
+        assert abs(lg - lr_) <= TOL * abs(lr_), (step, lg, lr_)
+    for p, q in zip(tr.get_parameters(), ref.params):
+        assert rel_err(p, q) <= TOL
+    _, logits = O.mlp_forward(cfg.dims, ref.params, x, t)
+    assert np.array_equal(tr.predict(x), np.argmax(logits, axis=1))
+    tr.close()
+
+
+def test_first_step_gradients_match_oracle(be):
+    """All GEMM orientations (forward, dW, dX) and db on one step."""
+    dims, B = [784, 512, 256, 10], 256
+    x, t, _ = make_batch(dims, B, 3)
+    tr = make(be, dims, B, "sgd", lr=0.0)
+    tr.step(x, t)
+    loss_ref, grads_ref, _ = O.mlp_forward_backward(dims, init_params(dims, 1), x, t)
+    for i, (g, r) in enumerate(zip(tr.get_grads(), grads_ref)):
+        assert rel_err(g, r) <= 1e-5, (i, rel_err(g, r))
+    tr.close()
+
+
+@pytest.mark.parametrize("name", ["sgdm_small", "sgd_small"])
+def test_golden_small_cases(be, golden, name):
+    """Goldens made from the reference's Python frontend (tests/golden)."""
+    case = golden[name]
+    dims = case["dims"]
+    x, t, _ = make_batch(dims, case["batch"], 0)
+    tr = make(be, dims, case["batch"], case["optimizer"], lr=case["lr"],
+              momentum=case.get("momentum", 0.0))
+    ref_losses = [np.frombuffer(bytes.fromhex(h), np.float32)[0] for h in case["loss_bits"][0]]
+    for step in range(case["steps"]):
+        lg = tr.step(x, t)
+        assert abs(lg - ref_losses[step]) <= TOL * abs(ref_losses[step]), (step, lg, ref_losses[step])
+    ref = np.load(os.path.join(os.path.dirname(__file__), "golden", f"{name}_final.npz"))
+    for i, p in enumerate(tr.get_parameters()):
+        assert rel_err(p, ref[f"arr_{i}"]) <= TOL
+    assert [int(v) for v in tr.predict(x)] == case["argmax"]
+    tr.close()
+
+
+def test_adamw_matches_oracle(be):
+    """configs[1]'s optimizer (AdamW lr 1e-3, wd 0.01) at reduced width, 20 steps."""
+    dims, B = [784, 256, 256, 10], 64
+    x, t, _ = make_batch(dims, B, 0)
+    tr = make(be, dims, B, "adamw", lr=1e-3, weight_decay=0.01)
+    ref = oracle_trainer(dims, "adamw", lr=1e-3, weight_decay=0.01)
+    for step in range(20):
+        lg, lr_ = tr.step(x, t), ref.step(x, t)
+        assert abs(lg - lr_) <= TOL * abs(lr_), (step, lg, lr_)
+    for p, q in zip(tr.get_parameters(), ref.params):
+        assert rel_err(p, q) <= TOL
+    tr.close()
+
+
+def test_c2_width_reduced_batch_matches_oracle(be):
+    """configs[2]'s model (784-8192-8192-10, SGD momentum 0.9, lr 0.01) with a
+    256-row batch so the oracle finishes in seconds: 2 steps."""
+    cfg = CONFIGS["c2"]
+    B = 256
+    x, t, _ = make_batch(cfg.dims, B, 0)
+    tr = make(be, cfg.dims, B, "sgd", lr=cfg.lr, momentum=cfg.momentum)
+    ref = oracle_trainer(cfg.dims, "sgd", lr=cfg.lr, momentum=cfg.momentum)
+    for step in range(2):
+        lg, lr_ = tr.step(x, t), ref.step(x, t)
+        assert abs(lg - lr_) <= TOL * abs(lr_), (step, lg, lr_)
+    for p, q in zip(tr.get_parameters(), ref.params):
+        assert rel_err(p, q) <= TOL
+    tr.close()
+
+
+def test_c2_full_size_properties(be):
+    """configs[2] at full size (B=4096): loss finite and decreasing over 4
+    steps, and two runs from the same state are bit-identical (determinism)."""
+    cfg = CONFIGS["c2"]
+    x, t, _ = make_batch(cfg.dims, cfg.batch, 0)
+    runs = []
+    for _ in range(2):
+        tr = make(be, cfg.dims, cfg.batch, "sgd", lr=cfg.lr, momentum=cfg.momentum)
+        losses = [tr.step(x, t) for _ in range(4)]
+        runs.append((losses, tr.get_parameters()[2][:64].copy()))
+        tr.close()
+    (l0, p0), (l1, p1) = runs
+    assert all(np.isfinite(l0)) and l0[-1] < l0[0]
+    assert l0 == l1 and np.array_equal(p0, p1)
+    assert abs(l0[0] - np.log(10.0)) < 0.1   # ~uniform logits at init
+
+
+def test_forward_only_and_validation(be):
+    from orcaml_b200.mlp import MlpTrainer
+    dims, B = [32, 16, 16, 10], 8
+    tr = make(be, dims, B, "sgd", lr=0.1)
+    x, t, _ = make_batch(dims, B, 0)
+    logits, loss = tr.forward(x, t)
+    ref_loss, ref_logits = O.mlp_forward(dims, init_params(dims, 1), x, t)
+    np.testing.assert_allclose(logits, ref_logits, rtol=1e-5, atol=1e-6)
+    assert abs(loss - ref_loss) <= 1e-5 * abs(ref_loss)
+    with pytest.raises(ValueError):
+        tr.step(x[:4], t[:4])
+    with pytest.raises(ValueError):
+        MlpTrainer(be, dims, B, optimizer="sgd", lr=-1.0)
+    with pytest.raises(ValueError):
+        MlpTrainer(be, dims, B, optimizer="sgd", lr=0.1, dampening=2.0)
+    with pytest.raises(TypeError):
+        MlpTrainer(be, dims, B, optimizer="sgd", lr=True)
+    with pytest.raises(ValueError):
+        MlpTrainer(be, dims, B, optimizer="adamw", lr=1e-3, betas=(1.0, 0.9))
+    tr.close()
