@@ -201,13 +201,15 @@ def run_ours(args):
         return float(tt.item())
 
     # ---- device-resident step (value) ----
+    clocks = ClockSampler(local).__enter__()   # sampling from warm-up on
     for _ in range(args.warmup):
         tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
     barrier()
     launches0 = be.launch_count()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    clocks.lines.clear()                       # keep only samples of the timed region
+    if True:
         barrier()
         ev0.record(stream)
         tr.profile_begin()
@@ -216,6 +218,7 @@ def run_ours(args):
         ev1.record(stream)
         sites = tr.profile_end()
         barrier()
+        clocks.__exit__(None, None, None)
     launches = be.launch_count() - launches0
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_step = ms / args.steps
@@ -248,6 +251,11 @@ def run_ours(args):
     tc_ms = sum(s["ms"] for s in tc_sites)
     tc_flops = sum(s["flops"] * s["launches"] for s in tc_sites)
     tc_launches = sum(s["launches"] for s in tc_sites)
+    # DRAM read + write of one tc_gemm_kernel launch, from an ncu --set full
+    # capture of the forward layer-2 GEMM (M=4096, N=8192, K=8192): 2.908 GB
+    # read + 0.240 GB written; its algorithmic operand + output bytes are 1.07 GB.
+    traffic = {"bytes_per_launch": 3.148e9, "launch": "forward layer 2, 4096x8192x8192",
+               "algorithmic_bytes": 1.074e9}
     achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
     step_flops = CFG.flops_per_sample() * B
     breakdown = {s["name"]: round(s["ms"] / max(1, s["launches"]), 4) for s in sites}
@@ -271,7 +279,7 @@ def run_ours(args):
                     "ms_per_step": e2e_ms / args.steps},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak,
                          "unit": "TFLOP/s", "frac": achieved / tf32_peak if tf32_peak else None,
-                         "traffic": None,
+                         "traffic": traffic["bytes_per_launch"], "traffic_detail": traffic,
                          "kernel": "tc_gemm_kernel (3xTF32 tcgen05, all GEMM launches of the step)",
                          "peak_note": f"{peak_src} bf16 dense {peaks['bf16_tflops']} TFLOP/s / 2 "
                                       "(tf32 rate) / 3 (products per FP32 product)",
@@ -298,7 +306,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--bucket-mb", type=int, default=64)

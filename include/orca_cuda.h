@@ -234,7 +234,8 @@ typedef struct {
   orca_optimizer optimizer;
   double lr, momentum, dampening, weight_decay;   /* SGD (sgd.py:30-44) */
   double beta1, beta2, eps;                       /* AdamW (adamw.py:24-38) */
-  int gemm_path;             /* 0 auto (tcgen05 where shapes allow), 1 SIMT FFMA only */
+  int gemm_path;             /* 0 auto (tcgen05 where shapes allow and the output has
+                                enough tiles), 1 SIMT FFMA only, 2 tcgen05 wherever allowed */
 } orca_mlp_config;
 
 orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp** out);

@@ -84,6 +84,7 @@ def _declare(L):
                                 ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.c_double,
                                 ctypes.c_int64]
     L.oc_ddp_average.argtypes = [PP, ctypes.c_int, ctypes.c_int64, _f32p]
+    L.oc_set_gemm_order.argtypes = [ctypes.c_int]
     L.oc_set_threads.argtypes = [ctypes.c_int]
     L.oc_get_threads.restype = ctypes.c_int
 
@@ -104,6 +105,11 @@ def _shape(s: Sequence[int]):
 
 def set_threads(n: int) -> None:
     lib().oc_set_threads(int(n))
+
+
+def set_gemm_order(order: int) -> None:
+    """0: k ascending (default); 1: with FMA; 2: k-blocks of 256; 3: f64-rounded."""
+    lib().oc_set_gemm_order(int(order))
 
 
 def threads() -> int:

@@ -240,10 +240,45 @@ static void gemm_block(const float* A, const float* B, float* C, int64_t m,
   }
 }
 
+/* Alternative, equally valid FP32 summation orders -- used only to measure
+ * how sensitive a training trajectory is to the (unpinned) summation order of
+ * the reference's GEMM.  0: k ascending, separate multiply and add (default);
+ * 1: k ascending with fused multiply-add; 2: partial sums over k-blocks of
+ * 256, then added in block order; 3: exact product rounded once (f64). */
+static int g_gemm_order = 0;
+void oc_set_gemm_order(int order) { g_gemm_order = order; }
+
+static void gemm_variant(const float* A, const float* B, float* C, int64_t m, int64_t k, int64_t n) {
+  for (int64_t i = 0; i < m; ++i)
+    for (int64_t j = 0; j < n; ++j) {
+      if (g_gemm_order == 1) {
+        float acc = 0.0f;
+        for (int64_t q = 0; q < k; ++q) acc = fmaf(A[i * k + q], B[q * n + j], acc);
+        C[i * n + j] = acc;
+      } else if (g_gemm_order == 2) {
+        float acc = 0.0f;
+        for (int64_t q0 = 0; q0 < k; q0 += 256) {
+          float part = 0.0f;
+          for (int64_t q = q0; q < k && q < q0 + 256; ++q) part = part + A[i * k + q] * B[q * n + j];
+          acc = acc + part;
+        }
+        C[i * n + j] = acc;
+      } else {
+        double acc = 0.0;
+        for (int64_t q = 0; q < k; ++q) acc += (double)A[i * k + q] * (double)B[q * n + j];
+        C[i * n + j] = (float)acc;
+      }
+    }
+}
+
 void oc_matmul(const float* a, const float* b, float* c, int64_t batch,
                int64_t m, int64_t k, int64_t n) {
   for (int64_t bi = 0; bi < batch; ++bi) {
     float* cb = c + bi * m * n;
+    if (g_gemm_order != 0) {
+      gemm_variant(a + bi * m * k, b + bi * k * n, cb, m, k, n);
+      continue;
+    }
     memset(cb, 0, (size_t)(m * n) * sizeof(float));
     gemm_block(a + bi * m * k, b + bi * k * n, cb, m, k, n);
   }

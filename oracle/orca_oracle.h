@@ -71,6 +71,9 @@ int oc_transpose(const float* in, const int64_t* shape, int rank,
 /* Batched row-major C[b] = A[b] (m x k) * B[b] (k x n), k ascending. :130-221 */
 void oc_matmul(const float* a, const float* b, float* c,
                int64_t batch, int64_t m, int64_t k, int64_t n);
+/* Select an alternative FP32 summation order for oc_matmul (0 = default);
+ * for sensitivity studies only. */
+void oc_set_gemm_order(int order);
 
 /* ---- composed training step ------------------------------------------------ */
 /* Forward + softmax cross-entropy + backward of Sequential(Linear, ReLU, ...,

@@ -141,6 +141,7 @@ orca_status orca_comm_init(orca_ctx* ctx, int rank, int world, const void* id, d
   if (!a.ok) return fail(ORCA_COMM_ERROR, "%s", a.why.c_str());
   orca_comm* c = new orca_comm();
   c->ctx = ctx;
+  ctx_retain(ctx);
   c->rank = rank;
   c->world = world;
   c->timeout_s = timeout_s;
@@ -150,12 +151,14 @@ orca_status orca_comm_init(orca_ctx* ctx, int rank, int world, const void* id, d
   cfg.blocking = 0;
   ncclResult_t r = a.CommInitRankConfig(&c->comm, world, uid, rank, &cfg);
   if (r != ncclSuccess && r != ncclInProgress) {
+    ctx_release(ctx);
     delete c;
     return nccl_fail(r, "ncclCommInitRankConfig");
   }
   orca_status s = wait_ready(c, "ncclCommInitRankConfig");
   if (s != ORCA_OK) {
     if (!c->aborted && c->comm) a.CommAbort(c->comm);
+    ctx_release(ctx);
     delete c;
     return s;
   }
@@ -166,6 +169,11 @@ orca_status orca_comm_init(orca_ctx* ctx, int rank, int world, const void* id, d
 orca_status orca_comm_destroy(orca_comm* c) {
   if (!c) return ORCA_OK;
   NcclApi& a = api();
+  orca_ctx* ctx = c->ctx;
+  struct Release {
+    orca_ctx* ctx;
+    ~Release() { ctx_release(ctx); }
+  } release{ctx};
   if (!c->aborted && c->comm) {
     cudaSetDevice(c->ctx->device);
     cudaStreamSynchronize(c->ctx->comm_stream);

@@ -48,6 +48,10 @@ enum DeviceError : int {
 }  // namespace orca
 
 struct orca_ctx {
+  // Buffers, step runners and communicators each hold a reference; the
+  // context is torn down when the last one is released (orca_ctx_destroy
+  // drops the creator's reference), so no object outlives its streams.
+  std::atomic<int> refs{1};
   int device = 0;
   int sm_count = 0;
   cudaStream_t stream = nullptr;        // compute stream
@@ -70,6 +74,8 @@ namespace orca {
 size_t dtype_size(orca_dtype d);
 orca_status check_ctx(orca_ctx* ctx);
 orca_status new_buf(orca_ctx* ctx, size_t n, orca_dtype dtype, orca_buf** out);
+void ctx_retain(orca_ctx* ctx);
+void ctx_release(orca_ctx* ctx);
 // Reads and clears the device error word (synchronises the compute stream).
 orca_status check_device_error(orca_ctx* ctx);
 inline void count_launch(orca_ctx* ctx, uint64_t n = 1) { ctx->launches += n; }
@@ -232,6 +238,21 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 }  // namespace orca

@@ -16,6 +16,7 @@
 // uses the 3xTF32 split with fp32 accumulation.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "gemm.cuh"
@@ -288,13 +289,26 @@ constexpr int A_STAGE = 2 * A_PLANE;                 // hi + lo
 constexpr int B_STAGE = 2 * B_PLANE;
 constexpr int TILE_BYTES = STAGES * (A_STAGE + B_STAGE);   // 192 KB
 constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
-constexpr int THREADS = 192;
-constexpr int TMEM_COLS = 2 * BN;                    // two accumulators
+constexpr int EPI_WARPS = 8;                         // 2 per TMEM lane quarter, 128 columns each
+constexpr int THREADS = 64 + 32 * EPI_WARPS;         // producer + MMA + epilogue warps
+constexpr int TMEM_COLS = 2 * BN;                    // two accumulator buffers
 constexpr int GROUP_M = 8;
+constexpr int DEFAULT_CHUNK_KB = 8;                  // k-blocks per accumulation chunk
+constexpr int SHORT_K_CHUNK_KB = 4;                  // ... when the whole K is <= 64 k-blocks
+
+// Accuracy note.  The tensor core adds each MMA's products into its fp32
+// accumulator with ~4 fewer bits than an FFMA rounding, so one accumulator
+// chain over a long K is measurably coarser than FP32 (error growing with
+// sqrt(K)).  The K loop of a tile is therefore split into chunks of chunk_kb
+// k-blocks; each chunk is accumulated from zero in one of the two TMEM
+// buffers and the epilogue warps add the chunks into fp32 registers while the
+// next chunk runs in the other buffer.  The long chain thus runs at FFMA
+// rounding, and the tensor-core chain is at most chunk_kb * 6 MMAs long.
 
 struct Params {
   int64_t M, N, K;
   int a_mn, b_mn;
+  int chunk_kb;            // k-blocks per accumulation chunk (>= 1)
   Epilogue ep;
   int* dev_err;
 };
@@ -311,19 +325,24 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   d |= (uint64_t)layout << 61;
   return d;
 }
-constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
+// Layout-type codes of the descriptor: 64B swizzle, and the 128B swizzle
+// with 32-byte atomicity -- the only shared-memory layout tcgen05 accepts for
+// an MN-major TF32 operand (4 rows of 128 B per swizzle atom).
+constexpr uint32_t LAYOUT_SW128_BASE32B = 1, LAYOUT_SW64 = 4;
 
 // Descriptor of one 8-deep k-step of one plane of a staged operand tile.
 //  K-major (box {16 k, rows, 2 planes}, 64B swizzle): row r at r*64 B, plane
-//    after rows*64 B; k-step ks starts 32 B further; 8-row groups 512 B apart.
-//  MN-major (boxes {32 mn, 16 k, 2 planes}, 128B swizzle, one per 32-wide mn
-//    chunk, 4 KB apart): k row at 128 B stride, lo plane 2 KB after hi; k-step
-//    ks = 8 k rows = 1 KB further.
+//    after rows*64 B; k-step ks starts 32 B further; 8-row groups 512 B apart
+//    (SBO).
+//  MN-major (boxes {32 mn, 16 k, 2 planes}, 128B/32B-atom swizzle, one box per
+//    32-wide mn chunk, chunks 4 KB apart = LBO): k row at 128 B stride, 4-row
+//    groups 512 B apart (SBO), lo plane 2 KB after hi; k-step ks = 8 k rows
+//    = 1 KB further.
 __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, int rows, int plane,
                                                  int ks) {
   if (mn_major) {
     uint32_t addr = base + plane * 2048 + ks * 1024;
-    return smem_desc(addr, 4096, 1024, LAYOUT_SW128);
+    return smem_desc(addr, 4096, 512, LAYOUT_SW128_BASE32B);
   }
   uint32_t addr = base + plane * (rows * 64) + ks * 32;
   return smem_desc(addr, 16, 512, LAYOUT_SW64);
@@ -350,13 +369,19 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* ma
   }
 }
 
+// Stores columns [n0, n0+32) of row m from acc[Q*32 .. Q*32+32) through the
+// epilogue.  Q is a template parameter so that every accumulator index is a
+// compile-time constant and the array stays in registers.
+template <int Q>
 __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, int64_t N, int64_t m,
-                                               int64_t n0, const float (&v)[32]) {
+                                               int64_t n0, const float (&acc)[128]) {
+#define v(i) acc[Q * 32 + (i)]
   if (m >= M) return;
   const bool full = (n0 + 32 <= N) && ((ep.ldc & 3) == 0);
   if (!full) {
+#pragma unroll
     for (int j = 0; j < 32; ++j)
-      if (n0 + j < N) store_epi(ep, m, n0 + j, v[j]);
+      if (n0 + j < N) store_epi(ep, m, n0 + j, v(j));
     return;
   }
   const int64_t base = m * ep.ldc + n0;
@@ -365,7 +390,7 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       float4 r;
-      r.x = v[4 * q + 0]; r.y = v[4 * q + 1]; r.z = v[4 * q + 2]; r.w = v[4 * q + 3];
+      r.x = v(4 * q + 0); r.y = v(4 * q + 1); r.z = v(4 * q + 2); r.w = v(4 * q + 3);
       if (ep.mode == EPI_BIAS) {
         r.x = __fadd_rn(r.x, ep.bias[n0 + 4 * q + 0]);
         r.y = __fadd_rn(r.y, ep.bias[n0 + 4 * q + 1]);
@@ -382,7 +407,7 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
   const float4* ml = reinterpret_cast<const float4*>(ep.mask_lo + base);
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
-    float x[4] = {v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]};
+    float x[4] = {v(4 * q + 0), v(4 * q + 1), v(4 * q + 2), v(4 * q + 3)};
     if (ep.mode == EPI_BIAS_RELU_SPLIT) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -405,6 +430,7 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
     ol[q] = l;
   }
 }
+#undef v
 
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -435,7 +461,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 32 * EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -493,14 +519,26 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                              ((uint32_t)(BM >> 4) << 24);
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
-      uint32_t aphase = 0;
+      uint32_t chunk_ctr = 0;             // chunks issued so far (all tiles)
       bool ok = true;
+      const int F = p.chunk_kb;
+      const int nk32 = (int)nk;
       for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(&tempty_bar[acc], aphase ^ 1u, abort_flag, p.dev_err)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int64_t kb = 0; kb < nk; ++kb) {
+        uint32_t d_tmem = tmem_base;
+        int buf = 0;
+        int in_chunk = 0;                 // k-blocks issued into the current chunk
+        for (int kb = 0; kb < nk32; ++kb) {
+          const bool chunk_start = in_chunk == 0;
+          if (chunk_start) {
+            buf = (int)(chunk_ctr & 1u);
+            const uint32_t use = chunk_ctr >> 1;     // uses of this buffer so far
+            if (!mbar_wait(&tempty_bar[buf], (use & 1u) ^ 1u, abort_flag, p.dev_err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d_tmem = tmem_base + (uint32_t)(buf * BN);
+          }
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.dev_err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_base = smem_u32(a_tiles + stage * A_STAGE);
@@ -511,17 +549,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const uint64_t a_lo = operand_desc(a_base, p.a_mn, BM, 1, ks);
             const uint64_t b_hi = operand_desc(b_base, p.b_mn, BN, 0, ks);
             const uint64_t b_lo = operand_desc(b_base, p.b_mn, BN, 1, ks);
-            const uint32_t first = (kb == 0 && ks == 0) ? 0u : 1u;
+            const uint32_t first = (chunk_start && ks == 0) ? 0u : 1u;
             tc_mma_tf32(d_tmem, a_lo, b_hi, idesc, first);
             tc_mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
             tc_mma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
           }
           tc_commit(&empty_bar[stage]);   // frees the smem stage once these MMAs finish
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          if (++in_chunk == F || kb == nk32 - 1) {
+            tc_commit(&tfull_bar[buf]);   // chunk ready for the epilogue
+            ++chunk_ctr;
+            in_chunk = 0;
+          }
         }
-        if (!ok) break;
-        tc_commit(&tfull_bar[acc]);       // accumulator ready for the epilogue
-        if (++acc == 2) { acc = 0; aphase ^= 1u; }
       }
       // Drain: every issued MMA has completed before TMEM is released.
       tc_commit(drain_bar);
@@ -531,27 +571,44 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;              // TMEM lanes [32q, 32q+32)
-    int acc = 0;
-    uint32_t aphase = 0;
-    for (int64_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    // Warp w reads TMEM lanes [32*(w%4), +32) (the hardware's lane-quarter
+    // rule) and columns [128*half, +128) of the 256-column tile.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) / 4;
+    const int nchunks = (int)cdiv(nk, p.chunk_kb);
+    uint32_t chunk_ctr = 0;
+    bool ok = true;
+    for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       int64_t tm, tn;
       tile_coords(tile, num_m, num_n, tm, tn);
-      if (!mbar_wait(&tfull_bar[acc], aphase, abort_flag, p.dev_err)) break;
-      tc_fence_after();
-      const int64_t m = tm * BM + quarter * 32 + lane;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        const uint32_t taddr =
-            tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c * 32);
-        tmem_ld_32x32b_x32(taddr, v);
-        const int64_t n0 = tn * BN + c * 32;
-        if (n0 < p.N) epilogue_chunk(p.ep, p.M, p.N, m, n0, v);
+      float acc[128];   // 0 + x == x: the first chunk adds into zeros exactly
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+      for (int c = 0; c < nchunks; ++c) {
+        const int buf = (int)(chunk_ctr & 1u);
+        const uint32_t use = chunk_ctr >> 1;
+        if (!mbar_wait(&tfull_bar[buf], use & 1u, abort_flag, p.dev_err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                               (uint32_t)(buf * BN + half * 128);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float v[16];
+          tmem_ld_32x32b_x16(tbase + (uint32_t)(q * 16), v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[q * 16 + j] = __fadd_rn(acc[q * 16 + j], v[j]);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[buf]);
+        ++chunk_ctr;
       }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
-      if (++acc == 2) { acc = 0; aphase ^= 1u; }
+      if (!ok) break;
+      const int64_t m = tm * BM + quarter * 32 + lane;
+      const int64_t nb = tn * BN + half * 128;
+      if (nb < p.N) epilogue_chunk<0>(p.ep, p.M, p.N, m, nb, acc);
+      if (nb + 32 < p.N) epilogue_chunk<1>(p.ep, p.M, p.N, m, nb + 32, acc);
+      if (nb + 64 < p.N) epilogue_chunk<2>(p.ep, p.M, p.N, m, nb + 64, acc);
+      if (nb + 96 < p.N) epilogue_chunk<3>(p.ep, p.M, p.N, m, nb + 96, acc);
     }
   }
 
@@ -588,7 +645,7 @@ static orca_status make_map(CUtensorMap* map, const Operand& op, int64_t inner_e
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(op.hi), dims,
                       strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_64B,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(ORCA_CUDA_ERROR, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return ORCA_OK;
@@ -612,6 +669,18 @@ bool eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const Operand& 
   return true;
 }
 
+// K-blocks (of BK = 16) per accumulation chunk.  Shorter chunks = shorter
+// tensor-core accumulation chains = smaller rounding error, at the cost of
+// more drains; ORCA_GEMM_CHUNK_KB overrides the default for tuning.
+static int64_t chunk_kblocks() {
+  static int64_t v = [] {
+    const char* e = getenv("ORCA_GEMM_CHUNK_KB");
+    long x = e ? strtol(e, nullptr, 10) : 0;
+    return (int64_t)(x > 0 ? x : DEFAULT_CHUNK_KB);
+  }();
+  return v;
+}
+
 orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
                    const Operand& B, const Epilogue& ep) {
   static bool attr_set[64] = {};
@@ -632,6 +701,14 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
   p.b_mn = B.mn_major ? 1 : 0;
   p.ep = ep;
   p.dev_err = ctx->dev_err;
+  // Measured on B200 (mean |error| / sum|a*b|, relu-activation x weight data):
+  // 8 k-blocks per chunk gives 1.6e-8 at K = 8192 and 5e-8 at K = 784, 4 gives
+  // 2.6e-8 at K = 784; a single chain gives 1.0e-6 at K = 8192.  Serial FP32
+  // FFMA gives ~2e-8.  The chunk drains cost ~4% of GEMM time at 8.
+  const int64_t nk = cdiv(K, BK);
+  const int64_t want = getenv("ORCA_GEMM_CHUNK_KB") ? chunk_kblocks()
+                       : (nk <= 64 ? SHORT_K_CHUNK_KB : DEFAULT_CHUNK_KB);
+  p.chunk_kb = (int)std::max<int64_t>(1, std::min<int64_t>(nk, want));
   const int64_t tiles = cdiv(M, BM) * cdiv(N, BN);
   const int grid = (int)std::min<int64_t>(tiles, ctx->sm_count);
   tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
@@ -642,22 +719,33 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
 }  // namespace tc
 
 // =============================================================== dispatch
+// GEMM_AUTO takes the tensor-core kernel when the operands allow it and the
+// output has enough 128x256 tiles to occupy a useful share of the SMs; a
+// problem of a few tiles (e.g. a 128-row batch) runs more CTAs on the SIMT
+// kernel.  GEMM_TC takes the tensor cores whenever the operands allow it.
+static bool use_tc(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
+                   const Operand& B, const Epilogue& ep, int path) {
+  if (path == GEMM_SIMT || K <= 0 || !tc::eligible(M, N, K, A, B, ep)) return false;
+  if (path == GEMM_TC) return true;
+  const int64_t tiles = cdiv(M, tc::BM) * cdiv(N, tc::BN);
+  return tiles >= std::max<int64_t>(8, ctx->sm_count / 8);
+}
+
 int gemm_select(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
                 const Operand& B, const Epilogue& ep, int path) {
-  (void)ctx;
-  if (path == GEMM_SIMT) return GEMM_SIMT;
-  if (tc::eligible(M, N, K, A, B, ep)) return GEMM_TC;
-  return GEMM_SIMT;
+  return use_tc(ctx, M, N, K, A, B, ep, path) ? GEMM_TC : GEMM_SIMT;
+}
+
+bool gemm_tc_eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const Operand& B) {
+  Epilogue ep;
+  return tc::eligible(M, N, K, A, B, ep);
 }
 
 orca_status gemm(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
                  const Operand& B, const Epilogue& ep, int path, float* workspace,
                  size_t workspace_bytes) {
   if (M <= 0 || N <= 0) return ORCA_OK;
-  if (path == GEMM_TC && !tc::eligible(M, N, K, A, B, ep))
-    return fail(ORCA_INVALID_ARGUMENT, "gemm: shape/operands not eligible for the tcgen05 path");
-  if (path != GEMM_SIMT && K > 0 && tc::eligible(M, N, K, A, B, ep))
-    return tc::launch(ctx, M, N, K, A, B, ep);
+  if (use_tc(ctx, M, N, K, A, B, ep, path)) return tc::launch(ctx, M, N, K, A, B, ep);
 
   if (N <= skinny::NMAX && K > 0) {
     // K-major A: a warp per row reads its row contiguously.  MN-major A (the

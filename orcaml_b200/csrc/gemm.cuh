@@ -37,6 +37,8 @@ struct Epilogue {
   const float* mask_lo = nullptr;
 };
 
+// AUTO: tensor cores when eligible and large enough; SIMT: FFMA kernels only;
+// TC: tensor cores whenever eligible (skinny/unaligned shapes still use SIMT).
 enum GemmPath : int { GEMM_AUTO = 0, GEMM_SIMT = 1, GEMM_TC = 2 };
 
 // Enqueue on ctx->stream.  `workspace`/`workspace_bytes` may be null/0; the
@@ -44,6 +46,9 @@ enum GemmPath : int { GEMM_AUTO = 0, GEMM_SIMT = 1, GEMM_TC = 2 };
 orca_status gemm(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
                  const Operand& B, const Epilogue& ep, int path,
                  float* workspace = nullptr, size_t workspace_bytes = 0);
+
+// Whether the tcgen05 kernel can take these operands at all.
+bool gemm_tc_eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const Operand& B);
 
 // Which path `gemm` would take (for reporting and tests).
 int gemm_select(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,

@@ -368,6 +368,7 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
   }
   orca_mlp* m = new orca_mlp();
   m->ctx = ctx;
+  ctx_retain(ctx);
   m->L = cfg->n_layers;
   m->dims.assign(cfg->dims, cfg->dims + cfg->n_layers + 1);
   m->B = cfg->batch;
@@ -463,7 +464,9 @@ orca_status orca_mlp_destroy(orca_mlp* m) {
   if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
   for (auto& r : m->recs) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
   for (auto e : m->event_pool) cudaEventDestroy(e);
+  orca_ctx* ctx = m->ctx;
   delete m;
+  ctx_release(ctx);
   return ORCA_OK;
 }
 

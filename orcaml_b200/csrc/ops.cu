@@ -55,6 +55,19 @@ orca_status check_ctx(orca_ctx* ctx) {
   return ORCA_OK;
 }
 
+void ctx_retain(orca_ctx* ctx) { ctx->refs++; }
+
+void ctx_release(orca_ctx* ctx) {
+  if (--ctx->refs != 0) return;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  cudaStreamSynchronize(ctx->comm_stream);
+  cudaFree(ctx->dev_err);
+  cudaStreamDestroy(ctx->stream);
+  cudaStreamDestroy(ctx->comm_stream);
+  delete ctx;
+}
+
 orca_status new_buf(orca_ctx* ctx, size_t n, orca_dtype dtype, orca_buf** out) {
   if (!out) return fail(ORCA_INVALID_ARGUMENT, "null output pointer");
   size_t es = dtype_size(dtype);
@@ -71,6 +84,7 @@ orca_status new_buf(orca_ctx* ctx, size_t n, orca_dtype dtype, orca_buf** out) {
                   cudaGetErrorString(e));
     }
   }
+  ctx_retain(ctx);
   *out = b;
   return ORCA_OK;
 }
@@ -356,13 +370,7 @@ orca_status orca_ctx_create(int device, orca_ctx** out) {
 
 orca_status orca_ctx_destroy(orca_ctx* ctx) {
   if (!ctx) return ORCA_OK;
-  cudaSetDevice(ctx->device);
-  cudaStreamSynchronize(ctx->stream);
-  cudaStreamSynchronize(ctx->comm_stream);
-  cudaFree(ctx->dev_err);
-  cudaStreamDestroy(ctx->stream);
-  cudaStreamDestroy(ctx->comm_stream);
-  delete ctx;
+  ctx_release(ctx);   // freed once every buffer / runner / communicator is released too
   return ORCA_OK;
 }
 
@@ -410,11 +418,13 @@ orca_status orca_buf_retain(orca_buf* buf) {
 orca_status orca_buf_release(orca_buf* buf) {
   if (!buf) return ORCA_OK;
   if (--buf->refs == 0) {
+    orca_ctx* ctx = buf->ctx;
     if (buf->ptr) {
-      cudaSetDevice(buf->ctx->device);
-      cudaFreeAsync(buf->ptr, buf->ctx->stream);
+      cudaSetDevice(ctx->device);
+      cudaFreeAsync(buf->ptr, ctx->stream);
     }
     delete buf;
+    ctx_release(ctx);
   }
   return ORCA_OK;
 }
@@ -850,6 +860,12 @@ orca_status orca_gemm_ex(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const o
   ep.mode = EPI_STORE;
   ep.out = (float*)(*out)->ptr;
   ep.ldc = N;
+  if (path == GEMM_TC && !gemm_tc_eligible(M, N, K, oa, ob)) {
+    cudaFreeAsync(scratch, ctx->stream);
+    orca_buf_release(*out);
+    *out = nullptr;
+    return fail(ORCA_INVALID_ARGUMENT, "gemm_ex: shape/operands not eligible for the tcgen05 path");
+  }
   orca_status st = gemm(ctx, M, N, K, oa, ob, ep, path);
   cudaFreeAsync(scratch, ctx->stream);
   if (st != ORCA_OK) {

@@ -57,11 +57,57 @@ def test_c0_twenty_steps_match_oracle(be, gemm_path):
     tr.close()
 
 
+def test_c0_teacher_forced_tensor_core_path(be):
+    """The tcgen05 path at c0, evaluated each step at the ORACLE's parameters
+    (teacher forcing): 20 steps of loss within 1e-6 and gradients within 1e-5.
+
+    A free-running 20-step trajectory can part from the oracle's when a ReLU
+    pre-activation lies within rounding distance of zero and the two GEMMs
+    round it to opposite signs (a mask flip); the oracle itself parts from its
+    own trajectory in the same way under other valid FP32 summation orders
+    (tests/test_oracle.py::test_oracle_order_sensitivity).  Evaluating at the
+    same parameters isolates the computation from that chaotic effect.  At
+    most one step may show a mask flip (a gradient deviation above 1e-5)."""
+    cfg = CONFIGS["c0"]
+    x, t, _ = make_batch(cfg.dims, cfg.batch, 0)
+    tr = make(be, cfg.dims, cfg.batch, "sgd", "tc", lr=0.0)
+    ref = oracle_trainer(cfg.dims, "sgd", lr=cfg.lr)
+    flips = 0
+    for step in range(20):
+        loss_ref, grads_ref, _ = O.mlp_forward_backward(cfg.dims, ref.params, x, t)
+        tr.set_parameters(ref.params)
+        lg = tr.step(x, t)
+        assert abs(lg - loss_ref) <= 1e-6 * abs(loss_ref), (step, lg, loss_ref)
+        errs = [rel_err(g, r) for g, r in zip(tr.get_grads(), grads_ref)]
+        if max(errs) > 1e-5:
+            flips += 1
+        ref.apply(grads_ref)
+    assert flips <= 1
+
+
+def test_c0_free_running_tensor_core_path(be):
+    """North-star bars on the tcgen05 path at c0: per-step loss within 1e-4 and
+    identical argmax after 20 steps; parameters stay within 1e-3 (a mask flip
+    moves them ~3e-4, see the teacher-forced test)."""
+    cfg = CONFIGS["c0"]
+    x, t, _ = make_batch(cfg.dims, cfg.batch, 0)
+    tr = make(be, cfg.dims, cfg.batch, "sgd", "tc", lr=cfg.lr)
+    ref = oracle_trainer(cfg.dims, "sgd", lr=cfg.lr)
+    for step in range(20):
+        lg, lr_ = tr.step(x, t), ref.step(x, t)
+        assert abs(lg - lr_) <= TOL * abs(lr_), (step, lg, lr_)
+    for p, q in zip(tr.get_parameters(), ref.params):
+        assert rel_err(p, q) <= 1e-3
+    _, logits = O.mlp_forward(cfg.dims, ref.params, x, t)
+    assert np.array_equal(tr.predict(x), np.argmax(logits, axis=1))
+    tr.close()
+
+
 def test_first_step_gradients_match_oracle(be):
     """All GEMM orientations (forward, dW, dX) and db on one step."""
     dims, B = [784, 512, 256, 10], 256
     x, t, _ = make_batch(dims, B, 3)
-    tr = make(be, dims, B, "sgd", lr=0.0)
+    tr = make(be, dims, B, "sgd", "tc", lr=0.0)
     tr.step(x, t)
     loss_ref, grads_ref, _ = O.mlp_forward_backward(dims, init_params(dims, 1), x, t)
     for i, (g, r) in enumerate(zip(tr.get_grads(), grads_ref)):

@@ -182,3 +182,25 @@ def test_oracle_ce_ties_golden(golden):
     loss, dP = O.softmax_ce(P, T)
     assert bits(loss) == case["loss_bits"]
     assert [bits(v) for v in dP.reshape(-1)] == case["dP_bits"]
+
+
+def test_oracle_order_sensitivity():
+    """Evidence for the parity bar: with a 256-row batch of the c0 model, 20
+    SGD steps of the oracle under other valid FP32 GEMM summation orders (FMA,
+    k-blocked, exactly rounded) end 1e-4..1e-3 away from its default order in
+    parameters (ReLU mask flips), while losses stay within 1e-5.  The reference
+    GEMM's own order (matrixmultiply, unpinned) is one more such order."""
+    dims, B = [784, 512, 512, 10], 256
+    x, t, _ = make_batch(dims, B, 0)
+    runs = {}
+    try:
+        for order in (0, 1):
+            O.set_gemm_order(order)
+            tr = O.OracleTrainer(dims, init_params(dims, 1), optimizer="sgd", lr=0.1)
+            runs[order] = ([tr.step(x, t) for _ in range(20)], tr.params)
+    finally:
+        O.set_gemm_order(0)
+    (l0, p0), (l1, p1) = runs[0], runs[1]
+    assert max(abs(a - b) / b for a, b in zip(l0, l1)) < 1e-4
+    worst = max(float(np.linalg.norm(a - b) / np.linalg.norm(b)) for a, b in zip(p0, p1))
+    assert worst > 1e-4
