@@ -210,6 +210,24 @@ orca_status orca_gemm_ex(orca_ctx* ctx, int64_t m, int64_t n, int64_t k, const o
 orca_status orca_softmax_ce_fwd_bwd(orca_ctx* ctx, const orca_buf* logits,
                                     const orca_buf* target, int64_t batch, int64_t classes,
                                     orca_buf** loss, orca_buf** dlogits);
+/* Softmax cross-entropy forward + backward that allocates nothing.  No
+ * counterpart in the reference: an addition for callers that cannot call
+ * cudaMalloc at this point -- code whose device memory is owned by another
+ * allocator (a framework's caching pool, a preallocated arena) and
+ * latency-bound loops, where a device allocation can synchronise the GPU or
+ * fragment the caller's pool.  The caller passes device pointers for every
+ * input and output: logits and target [batch, classes], loss [1], dlogits
+ * [batch, classes] (NULL for forward only).  The per-row scratch is a fixed
+ * device array of 2^20 rows (4 MiB, resident on every GPU that loads the
+ * library); larger batches are rejected with ORCA_INVALID_ARGUMENT.  The
+ * first call on a device looks up that array's device address (a one-time
+ * set-up, done with the device current); make this first call before any
+ * stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (other streams, other host threads with their own contexts on the same
+ * device) race on it. */
+orca_status orca_softmax_ce_fwd_bwd_noalloc(orca_ctx* ctx, const float* logits,
+                                            const float* target, int64_t batch, int64_t classes,
+                                            float* loss, float* dlogits);
 /* In-place optimizer updates with the reference's per-op f32 rounding
  * (python/orca/optim/sgd.py:55-79, adamw.py:75-99).  v / m may be NULL when
  * unused; first != 0 is SGD's first momentum step. */

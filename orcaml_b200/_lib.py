@@ -104,6 +104,8 @@ _SIGS = {
     "orca_gemm_ex": ([c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int, c_int,
                       PP], c_int),
     "orca_softmax_ce_fwd_bwd": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, PP, PP], c_int),
+    "orca_softmax_ce_fwd_bwd_noalloc": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+                                         c_void_p], c_int),
     "orca_sgd_step": ([c_void_p, c_void_p, c_void_p, c_void_p, c_double, c_double, c_double,
                        c_double, c_int], c_int),
     "orca_adamw_step": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_double, c_double,

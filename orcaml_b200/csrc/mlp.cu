@@ -922,6 +922,64 @@ orca_status orca_softmax_ce_fwd_bwd(orca_ctx* ctx, const orca_buf* logits, const
   return ORCA_OK;
 }
 
+// ---- softmax-CE without allocation ------------------------------------------
+// Row losses of orca_softmax_ce_fwd_bwd_noalloc live in this fixed device
+// array instead of a per-call allocation.  Every GPU that loads the library
+// holds it until the process exits.  Host code must not hand the symbol
+// itself to a kernel (on the host it is only a stand-in for the device
+// array); the device address is looked up once per device below.
+}  // extern "C"
+
+namespace orca {
+constexpr int64_t kCeScratchRows = int64_t(1) << 20;   // 4 MiB of f32 row losses
+static __device__ __align__(256) float g_ce_row_scratch[kCeScratchRows];
+static float* g_ce_scratch_addr[128] = {};              // per device, set once
+static std::mutex g_ce_scratch_mu;
+
+static orca_status ce_scratch_for(int device, float** out) {
+  if (device < 0 || device >= 128) return fail(ORCA_INVALID_ARGUMENT, "device index %d", device);
+  std::lock_guard<std::mutex> lk(g_ce_scratch_mu);
+  if (!g_ce_scratch_addr[device]) {
+    // The device must be current here (the caller has made it so).
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_ce_row_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(ORCA_CUDA_ERROR, "cudaGetSymbolAddress(row-loss scratch) failed: %s",
+                  cudaGetErrorString(e));
+    g_ce_scratch_addr[device] = static_cast<float*>(ptr);
+  }
+  *out = g_ce_scratch_addr[device];
+  return ORCA_OK;
+}
+}  // namespace orca
+
+extern "C" {
+
+orca_status orca_softmax_ce_fwd_bwd_noalloc(orca_ctx* ctx, const float* logits,
+                                            const float* target, int64_t batch, int64_t classes,
+                                            float* loss, float* dlogits) {
+  ORCA_TRY(check_ctx(ctx));   // makes ctx->device current
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (!logits || !target || !loss) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (batch < 1 || classes < 1) return fail(ORCA_INVALID_ARGUMENT, "empty batch");
+  if (batch > kCeScratchRows)
+    return fail(ORCA_INVALID_ARGUMENT,
+                "batch %lld exceeds the %lld rows of the fixed no-allocation scratch; "
+                "use orca_softmax_ce_fwd_bwd for larger batches",
+                (long long)batch, (long long)kCeScratchRows);
+  float* rows = nullptr;
+  ORCA_TRY(ce_scratch_for(ctx->device, &rows));
+  // Every row of the scratch that ce_loss_kernel reads is written first by
+  // ce_kernel on the same stream, so nothing needs clearing between calls.
+  const float inv_b = 1.0f / (float)batch;
+  ce_kernel<<<(unsigned)cdiv(batch, 128), 128, 0, ctx->stream>>>(logits, target, batch, classes,
+                                                                inv_b, dlogits, rows);
+  ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(rows, batch, inv_b, loss);
+  count_launch(ctx, 2);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
 orca_status orca_sgd_step(orca_ctx* ctx, orca_buf* p, const orca_buf* g, orca_buf* v, double lr,
                           double momentum, double dampening, double weight_decay, int first) {
   ORCA_TRY(check_ctx(ctx));
