@@ -79,6 +79,16 @@ orca_status orca_ctx_destroy(orca_ctx* ctx);
 orca_status orca_ctx_sync(orca_ctx* ctx, double timeout_s);
 /* Backend::device (trait :24). */
 orca_status orca_ctx_device(const orca_ctx* ctx, int* device);
+/* Deadline in seconds for every call that waits on the device (default 600).
+ * A wait past it returns ORCA_TIMEOUT instead of blocking; a trainer with a
+ * communicator attached then aborts the communicator (a peer has gone). */
+orca_status orca_ctx_set_timeout(orca_ctx* ctx, double seconds);
+/* Runs a one-warp kernel whose mbarrier wait nothing completes, bounded by
+ * limit_s (0 < limit_s <= 10): the wait runs out, the kernel records the
+ * timeout and returns, and this call returns ORCA_TIMEOUT with the context
+ * still usable.  Exercises the bounded-wait path of the device code without
+ * any fault. */
+orca_status orca_ctx_selftest_wait_timeout(orca_ctx* ctx, double limit_s);
 /* The compute stream (a cudaStream_t), for callers that interoperate. */
 void* orca_ctx_stream(orca_ctx* ctx);
 /* Number of this library's kernels launched on ctx so far. */

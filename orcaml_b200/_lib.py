@@ -71,6 +71,8 @@ _SIGS = {
     "orca_ctx_destroy": ([c_void_p], c_int),
     "orca_ctx_sync": ([c_void_p, c_double], c_int),
     "orca_ctx_device": ([c_void_p, ctypes.POINTER(c_int)], c_int),
+    "orca_ctx_set_timeout": ([c_void_p, c_double], c_int),
+    "orca_ctx_selftest_wait_timeout": ([c_void_p, c_double], c_int),
     "orca_ctx_stream": ([c_void_p], c_void_p),
     "orca_ctx_launch_count": ([c_void_p], c_uint64),
     "orca_buf_retain": ([c_void_p], c_int),

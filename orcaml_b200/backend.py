@@ -83,6 +83,16 @@ class CudaBackend:
     def synchronize(self, timeout_s: float = 600.0):
         L.check(L.load().orca_ctx_sync(self._ctx, float(timeout_s)))
 
+    def set_timeout(self, seconds: float):
+        """Deadline for every call that waits on the device; past it the call
+        raises OrcaTimeout instead of blocking."""
+        L.check(L.load().orca_ctx_set_timeout(self._ctx, float(seconds)))
+
+    def selftest_wait_timeout(self, limit_s: float):
+        """Runs a device wait that nothing completes, bounded by limit_s; raises
+        OrcaTimeout (the expected outcome) and leaves the context usable."""
+        L.check(L.load().orca_ctx_selftest_wait_timeout(self._ctx, float(limit_s)))
+
     def launch_count(self) -> int:
         return int(L.load().orca_ctx_launch_count(self._ctx))
 

@@ -26,6 +26,8 @@ struct orca_comm {
   int rank = 0, world = 1;
   double timeout_s = 600.0;
   bool aborted = false;
+  cudaEvent_t ev_in = nullptr;    // compute stream -> comm stream ordering
+  cudaEvent_t ev_out = nullptr;   // comm stream -> compute stream ordering
 };
 
 namespace orca {
@@ -156,8 +158,14 @@ orca_status orca_comm_init(orca_ctx* ctx, int rank, int world, const void* id, d
     return nccl_fail(r, "ncclCommInitRankConfig");
   }
   orca_status s = wait_ready(c, "ncclCommInitRankConfig");
+  if (s == ORCA_OK &&
+      (cudaEventCreateWithFlags(&c->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+       cudaEventCreateWithFlags(&c->ev_out, cudaEventDisableTiming) != cudaSuccess))
+    s = fail(ORCA_CUDA_ERROR, "event creation failed");
   if (s != ORCA_OK) {
     if (!c->aborted && c->comm) a.CommAbort(c->comm);
+    if (c->ev_in) cudaEventDestroy(c->ev_in);
+    if (c->ev_out) cudaEventDestroy(c->ev_out);
     ctx_release(ctx);
     delete c;
     return s;
@@ -169,28 +177,33 @@ orca_status orca_comm_init(orca_ctx* ctx, int rank, int world, const void* id, d
 orca_status orca_comm_destroy(orca_comm* c) {
   if (!c) return ORCA_OK;
   NcclApi& a = api();
-  orca_ctx* ctx = c->ctx;
   struct Release {
-    orca_ctx* ctx;
-    ~Release() { ctx_release(ctx); }
-  } release{ctx};
+    orca_comm* c;
+    ~Release() {
+      if (c->ev_in) cudaEventDestroy(c->ev_in);
+      if (c->ev_out) cudaEventDestroy(c->ev_out);
+      ctx_release(c->ctx);
+      delete c;
+    }
+  } release{c};
   if (!c->aborted && c->comm) {
     cudaSetDevice(c->ctx->device);
-    cudaStreamSynchronize(c->ctx->comm_stream);
+    // Bounded: a collective that a vanished peer never completes must not
+    // hang teardown; the communicator is aborted instead.
+    if (sync_stream_for(c->ctx, c->ctx->comm_stream, c->timeout_s) != ORCA_OK) {
+      a.CommAbort(c->comm);
+      c->aborted = true;
+      return fail(ORCA_TIMEOUT, "comm destroy: collectives pending after %.1f s; aborted",
+                  c->timeout_s);
+    }
     ncclResult_t r = a.CommFinalize(c->comm);
     if (r != ncclSuccess && r != ncclInProgress) {
       a.CommAbort(c->comm);
-      delete c;
       return nccl_fail(r, "ncclCommFinalize");
     }
-    orca_status s = wait_ready(c, "ncclCommFinalize");   // aborts on timeout
-    if (s != ORCA_OK) {
-      delete c;
-      return s;
-    }
+    ORCA_TRY(wait_ready(c, "ncclCommFinalize"));   // aborts on timeout
     a.CommDestroy(c->comm);
   }
-  delete c;
   return ORCA_OK;
 }
 
@@ -206,14 +219,11 @@ orca_status orca_comm_allreduce_avg(orca_comm* c, float* dev_ptr, size_t n) {
   if (!c) return fail(ORCA_INVALID_ARGUMENT, "null communicator");
   ORCA_TRY(check_ctx(c->ctx));
   std::lock_guard<std::mutex> lk(c->ctx->mu);
-  cudaEvent_t ev;
-  ORCA_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-  cudaEventRecord(ev, c->ctx->stream);
-  cudaStreamWaitEvent(c->ctx->comm_stream, ev, 0);
+  ORCA_CUDA_TRY(cudaEventRecord(c->ev_in, c->ctx->stream));
+  ORCA_CUDA_TRY(cudaStreamWaitEvent(c->ctx->comm_stream, c->ev_in, 0));
   orca_status s = comm_allreduce_avg_stream(c, dev_ptr, n, c->ctx->comm_stream);
-  cudaEventRecord(ev, c->ctx->comm_stream);
-  cudaStreamWaitEvent(c->ctx->stream, ev, 0);
-  cudaEventDestroy(ev);
+  ORCA_CUDA_TRY(cudaEventRecord(c->ev_out, c->ctx->comm_stream));
+  ORCA_CUDA_TRY(cudaStreamWaitEvent(c->ctx->stream, c->ev_out, 0));
   return s;
 }
 

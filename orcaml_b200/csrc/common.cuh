@@ -57,6 +57,8 @@ struct orca_ctx {
   cudaStream_t stream = nullptr;        // compute stream
   cudaStream_t comm_stream = nullptr;   // collectives
   int* dev_err = nullptr;               // device error word (DeviceError)
+  double sync_timeout_s = 600.0;        // bound on every synchronising call
+  cudaEvent_t sync_event = nullptr;
   std::mutex mu;
   std::atomic<uint64_t> launches{0};
 };
@@ -76,6 +78,11 @@ orca_status check_ctx(orca_ctx* ctx);
 orca_status new_buf(orca_ctx* ctx, size_t n, orca_dtype dtype, orca_buf** out);
 void ctx_retain(orca_ctx* ctx);
 void ctx_release(orca_ctx* ctx);
+// Waits for a stream with a deadline (never blocks forever); ORCA_TIMEOUT
+// when the deadline passes.  sync_stream uses the compute stream and the
+// context's deadline.
+orca_status sync_stream(orca_ctx* ctx);
+orca_status sync_stream_for(orca_ctx* ctx, cudaStream_t stream, double timeout_s);
 // Reads and clears the device error word (synchronises the compute stream).
 orca_status check_device_error(orca_ctx* ctx);
 inline void count_launch(orca_ctx* ctx, uint64_t n = 1) { ctx->launches += n; }
@@ -148,17 +155,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity.  Returns false (and
 // raises *abort) when the bound runs out or another role already aborted.
+// The clock and the abort flag are checked every 64 polls only; sleep_ns > 0
+// backs off between polls (for waiters whose latency is not critical, so the
+// issue slots stay with the MMA warp).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort, int* dev_err) {
+                                          volatile int* abort, int* dev_err,
+                                          unsigned sleep_ns = 0,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
-  while (true) {
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (global_ns() - t0 > kWaitLimitNs) {
-      *abort = 1;
-      if (dev_err) atomicExch(dev_err, DEV_WAIT_TIMEOUT);
-      return false;
+    if (sleep_ns) __nanosleep(sleep_ns);
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > limit_ns) {
+        *abort = 1;
+        if (dev_err) atomicExch(dev_err, DEV_WAIT_TIMEOUT);
+        return false;
+      }
     }
   }
 }

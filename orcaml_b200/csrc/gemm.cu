@@ -492,7 +492,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         int64_t tm, tn;
         tile_coords(tile, num_m, num_n, tm, tn);
         for (int64_t kb = 0; kb < nk; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.dev_err)) { ok = false; break; }
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.dev_err, 20)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[stage], A_STAGE + B_STAGE);
           load_operand(a_tiles + stage * A_STAGE, &map_a, &full_bar[stage], p.a_mn, BM, tm * BM,
                        kb * BK);
@@ -587,7 +587,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       for (int c = 0; c < nchunks; ++c) {
         const int buf = (int)(chunk_ctr & 1u);
         const uint32_t use = chunk_ctr >> 1;
-        if (!mbar_wait(&tfull_bar[buf], use & 1u, abort_flag, p.dev_err)) { ok = false; break; }
+        if (!mbar_wait(&tfull_bar[buf], use & 1u, abort_flag, p.dev_err, 64)) { ok = false; break; }
         tc_fence_after();
         const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) +
                                (uint32_t)(buf * BN + half * 128);

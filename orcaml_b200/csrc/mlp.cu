@@ -342,6 +342,24 @@ static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad);
 static orca_status mlp_backward_impl(orca_mlp* m);
 static orca_status mlp_update_impl(orca_mlp* m);
 
+// Waits for the step's work with the context's deadline.  A deadline that
+// passes while a communicator is attached means a peer stopped taking part
+// (the compute stream waits on the gradient all-reduce): the communicator is
+// aborted, which ends its pending collective, the streams drain (bounded) and
+// the caller gets ORCA_TIMEOUT.  The trainer is then detached from the
+// communicator; its parameters are those of the last completed step or a
+// partially updated state and must be reloaded before further use.
+static orca_status finish_sync(orca_mlp* m) {
+  const orca_status s = sync_stream(m->ctx);
+  if (s != ORCA_TIMEOUT || !m->comm) return s;
+  const std::string why = orca_last_error();
+  orca_comm_abort(m->comm);
+  m->comm = nullptr;
+  sync_stream_for(m->ctx, m->ctx->comm_stream, 30.0);
+  sync_stream_for(m->ctx, m->ctx->stream, 30.0);
+  return fail(ORCA_TIMEOUT, "%s; communicator aborted (a peer stopped responding)", why.c_str());
+}
+
 extern "C" {
 
 orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp** out) {
@@ -448,7 +466,7 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
       return cleanup(fail(ORCA_CUDA_ERROR, "event creation failed"));
   if (cudaEventCreateWithFlags(&m->ev_comm_done, cudaEventDisableTiming) != cudaSuccess)
     return cleanup(fail(ORCA_CUDA_ERROR, "event creation failed"));
-  if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(ORCA_CUDA_ERROR, "init sync"));
+  if (sync_stream(ctx) != ORCA_OK) return cleanup(ORCA_CUDA_ERROR);
   *out = m;
   return ORCA_OK;
 }
@@ -456,8 +474,8 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
 orca_status orca_mlp_destroy(orca_mlp* m) {
   if (!m) return ORCA_OK;
   cudaSetDevice(m->ctx->device);
-  cudaStreamSynchronize(m->ctx->stream);
-  cudaStreamSynchronize(m->ctx->comm_stream);
+  sync_stream_for(m->ctx, m->ctx->stream, m->ctx->sync_timeout_s);
+  sync_stream_for(m->ctx, m->ctx->comm_stream, m->ctx->sync_timeout_s);
   for (void* p : m->allocs) cudaFree(p);
   for (int l = 0; l < 64; ++l)
     if (m->ev_layer[l]) cudaEventDestroy(m->ev_layer[l]);
@@ -501,7 +519,7 @@ orca_status orca_mlp_set_param(orca_mlp* m, int index, const float* host, int64_
     ORCA_CUDA_TRY(cudaMemcpyAsync(m->bias[l], host, (size_t)n * 4, cudaMemcpyHostToDevice,
                                   m->ctx->stream));
   }
-  ORCA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+  ORCA_TRY(finish_sync(m));
   return ORCA_OK;
 }
 
@@ -525,7 +543,7 @@ orca_status orca_mlp_get_param(orca_mlp* m, int index, float* host, int64_t nume
     ORCA_CUDA_TRY(cudaMemcpyAsync(host, m->bias[l], (size_t)n * 4, cudaMemcpyDeviceToHost,
                                   m->ctx->stream));
   }
-  ORCA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+  ORCA_TRY(finish_sync(m));
   return check_device_error(m->ctx);
 }
 
@@ -537,7 +555,7 @@ orca_status orca_mlp_get_grad(orca_mlp* m, int index, float* host, int64_t numel
   std::lock_guard<std::mutex> lk(m->ctx->mu);
   ORCA_CUDA_TRY(cudaMemcpyAsync(host, m->grads + m->p_off[index], (size_t)n * 4,
                                 cudaMemcpyDeviceToHost, m->ctx->stream));
-  ORCA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+  ORCA_TRY(finish_sync(m));
   return check_device_error(m->ctx);
 }
 
@@ -589,7 +607,7 @@ orca_status orca_mlp_step(orca_mlp* m, const float* x, const float* t, float* lo
   ORCA_TRY(step_device_locked(m, m->x_stage, m->t_buf, nullptr));
   if (loss) {
     ORCA_CUDA_TRY(cudaMemcpyAsync(loss, m->loss, 4, cudaMemcpyDeviceToHost, ctx->stream));
-    ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    ORCA_TRY(finish_sync(m));
     return check_device_error(ctx);
   }
   return ORCA_OK;
@@ -623,7 +641,7 @@ orca_status orca_mlp_forward(orca_mlp* m, const float* x, const float* t, float*
                                   ctx->stream));
   if (loss && t)
     ORCA_CUDA_TRY(cudaMemcpyAsync(loss, m->loss, 4, cudaMemcpyDeviceToHost, ctx->stream));
-  ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  ORCA_TRY(finish_sync(m));
   return check_device_error(ctx);
 }
 
@@ -640,7 +658,7 @@ orca_status orca_mlp_profile_end(orca_mlp* m, int* n_sites) {
   ORCA_TRY(check_ctx(m->ctx));
   std::lock_guard<std::mutex> lk(m->ctx->mu);
   m->profiling = false;
-  ORCA_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+  ORCA_TRY(finish_sync(m));
   for (auto& r : m->recs) {
     float ms = 0;
     if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {

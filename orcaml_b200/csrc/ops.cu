@@ -60,9 +60,12 @@ void ctx_retain(orca_ctx* ctx) { ctx->refs++; }
 void ctx_release(orca_ctx* ctx) {
   if (--ctx->refs != 0) return;
   cudaSetDevice(ctx->device);
-  cudaStreamSynchronize(ctx->stream);
-  cudaStreamSynchronize(ctx->comm_stream);
+  // Bounded: a stream that never drains (a peer gone mid-collective whose
+  // communicator was not aborted) must not hang the caller's teardown.
+  sync_stream_for(ctx, ctx->stream, ctx->sync_timeout_s);
+  sync_stream_for(ctx, ctx->comm_stream, ctx->sync_timeout_s);
   cudaFree(ctx->dev_err);
+  if (ctx->sync_event) cudaEventDestroy(ctx->sync_event);
   cudaStreamDestroy(ctx->stream);
   cudaStreamDestroy(ctx->comm_stream);
   delete ctx;
@@ -89,10 +92,29 @@ orca_status new_buf(orca_ctx* ctx, size_t n, orca_dtype dtype, orca_buf** out) {
   return ORCA_OK;
 }
 
+orca_status sync_stream(orca_ctx* ctx) {
+  return sync_stream_for(ctx, ctx->stream, ctx->sync_timeout_s);
+}
+
+orca_status sync_stream_for(orca_ctx* ctx, cudaStream_t stream, double timeout_s) {
+  ORCA_CUDA_TRY(cudaEventRecord(ctx->sync_event, stream));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0;; ++it) {
+    const cudaError_t e = cudaEventQuery(ctx->sync_event);
+    if (e == cudaSuccess) return ORCA_OK;
+    if (e != cudaErrorNotReady)
+      return fail(ORCA_CUDA_ERROR, "stream error: %s", cudaGetErrorString(e));
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s)
+      return fail(ORCA_TIMEOUT, "device work still pending after %.1f s", timeout_s);
+    if (it > 1000) std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
 orca_status check_device_error(orca_ctx* ctx) {
   int h = 0;
   ORCA_CUDA_TRY(cudaMemcpyAsync(&h, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
-  ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  ORCA_TRY(sync_stream(ctx));
   if (h != DEV_OK) {
     ORCA_CUDA_TRY(cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), ctx->stream));
     if (h == DEV_WAIT_TIMEOUT)
@@ -310,6 +332,22 @@ __global__ void nonfinite_kernel(const float* in, int64_t n, int* flag) {
     if (!isfinite(in[i])) { atomicExch(flag, 1); return; }
 }
 
+// Waits on an mbarrier that nothing arrives at, with a bound of limit_ns: the
+// wait must run out, record DEV_WAIT_TIMEOUT and return -- the same bounded
+// wait the GEMM's roles use, exercised without any fault.
+__global__ void selftest_wait_kernel(int* dev_err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, dev_err, 100, limit_ns);
+  __syncthreads();
+}
+
 }  // namespace orca
 
 using namespace orca;
@@ -355,6 +393,7 @@ orca_status orca_ctx_create(int device, orca_ctx** out) {
   c->sm_count = prop.multiProcessorCount;
   ORCA_CUDA_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   ORCA_CUDA_TRY(cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking));
+  ORCA_CUDA_TRY(cudaEventCreateWithFlags(&c->sync_event, cudaEventDisableTiming));
   ORCA_CUDA_TRY(cudaMalloc(&c->dev_err, sizeof(int)));
   ORCA_CUDA_TRY(cudaMemset(c->dev_err, 0, sizeof(int)));
   // Keep freed stream-ordered allocations in the pool instead of returning
@@ -376,27 +415,27 @@ orca_status orca_ctx_destroy(orca_ctx* ctx) {
 
 orca_status orca_ctx_sync(orca_ctx* ctx, double timeout_s) {
   ORCA_TRY(check_ctx(ctx));
-  if (timeout_s <= 0) timeout_s = 600.0;
-  cudaEvent_t ev;
-  ORCA_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-  cudaEventRecord(ev, ctx->stream);
-  auto t0 = std::chrono::steady_clock::now();
-  while (true) {
-    cudaError_t e = cudaEventQuery(ev);
-    if (e == cudaSuccess) break;
-    if (e != cudaErrorNotReady) {
-      cudaEventDestroy(ev);
-      return fail(ORCA_CUDA_ERROR, "stream error: %s", cudaGetErrorString(e));
-    }
-    double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-    if (el > timeout_s) {
-      cudaEventDestroy(ev);
-      return fail(ORCA_TIMEOUT, "orca_ctx_sync: work still pending after %.1f s", timeout_s);
-    }
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
-  }
-  cudaEventDestroy(ev);
+  if (timeout_s <= 0) timeout_s = ctx->sync_timeout_s;
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  ORCA_TRY(sync_stream_for(ctx, ctx->stream, timeout_s));
   return check_device_error(ctx);
+}
+
+orca_status orca_ctx_set_timeout(orca_ctx* ctx, double seconds) {
+  if (!ctx || !(seconds > 0)) return fail(ORCA_INVALID_ARGUMENT, "timeout must be positive");
+  ctx->sync_timeout_s = seconds;
+  return ORCA_OK;
+}
+
+orca_status orca_ctx_selftest_wait_timeout(orca_ctx* ctx, double limit_s) {
+  ORCA_TRY(check_ctx(ctx));
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (!(limit_s > 0) || limit_s > 10.0)
+    return fail(ORCA_INVALID_ARGUMENT, "limit must be in (0, 10] seconds");
+  selftest_wait_kernel<<<1, 32, 0, ctx->stream>>>(ctx->dev_err, (uint64_t)(limit_s * 1e9));
+  count_launch(ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return check_device_error(ctx);   // ORCA_TIMEOUT when the wait ran out, as it must
 }
 
 orca_status orca_ctx_device(const orca_ctx* ctx, int* device) {
@@ -459,7 +498,7 @@ orca_status orca_from_f32_slice(orca_ctx* ctx, const int64_t* dims, int rank, co
   if (n) {
     ORCA_CUDA_TRY(cudaMemcpyAsync((*out)->ptr, data, (size_t)n * 4, cudaMemcpyHostToDevice,
                                   ctx->stream));
-    ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));   // host memory may be freed on return
+    ORCA_TRY(sync_stream(ctx));   // host memory may be freed on return
   }
   return ORCA_OK;
 }
@@ -473,7 +512,7 @@ orca_status orca_to_f32_vec(orca_ctx* ctx, const orca_buf* buf, float* dst, size
     return fail(ORCA_SHAPE_MISMATCH, "to_f32_vec: buffer has %zu elements, dst %zu", buf->n, n_elems);
   if (n_elems)
     ORCA_CUDA_TRY(cudaMemcpyAsync(dst, buf->ptr, n_elems * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  ORCA_TRY(sync_stream(ctx));
   return check_device_error(ctx);
 }
 
@@ -490,7 +529,7 @@ orca_status orca_from_bytes(orca_ctx* ctx, const int64_t* dims, int rank, const 
   ORCA_TRY(new_buf(ctx, (size_t)n, dtype, out));
   if (n_bytes) {
     ORCA_CUDA_TRY(cudaMemcpyAsync((*out)->ptr, bytes, n_bytes, cudaMemcpyHostToDevice, ctx->stream));
-    ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    ORCA_TRY(sync_stream(ctx));
   }
   return ORCA_OK;
 }
@@ -503,7 +542,7 @@ orca_status orca_to_bytes(orca_ctx* ctx, const orca_buf* buf, void* dst, size_t 
     return fail(ORCA_SHAPE_MISMATCH, "to_bytes: size mismatch");
   if (n_bytes)
     ORCA_CUDA_TRY(cudaMemcpyAsync(dst, buf->ptr, n_bytes, cudaMemcpyDeviceToHost, ctx->stream));
-  ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  ORCA_TRY(sync_stream(ctx));
   return check_device_error(ctx);
 }
 
@@ -933,7 +972,7 @@ orca_status orca_has_nan_or_inf(orca_ctx* ctx, const orca_buf* x, orca_dtype dty
   int h = 0;
   ORCA_CUDA_TRY(cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
   cudaFreeAsync(flag, ctx->stream);
-  ORCA_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  ORCA_TRY(sync_stream(ctx));
   *result = h;
   return ORCA_OK;
 }

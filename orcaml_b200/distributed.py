@@ -78,15 +78,51 @@ def _recv_exact(conn: socket.socket, n: int) -> bytes:
     return bytes(buf)
 
 
-def exchange_id(rank: int, world_size: int, master_addr: str, timeout: float, make_id) -> bytes:
-    """Rank 0 calls make_id() and sends the bytes to every worker over TCP.
+class PeerLinks:
+    """The rendezvous sockets, kept open as a liveness channel.
+
+    Rank 0 holds one connection per worker, each worker one to rank 0 (the
+    reference's star, python/orca/distributed.py:161-210).  Nothing is sent on
+    them after the rendezvous, so a readable socket means its peer closed it
+    or exited: `check()` raises RuntimeError before the next step launches any
+    collective that the peer would never join."""
+
+    def __init__(self, rank: int, conns):
+        self.rank = rank
+        self.conns = list(conns)
+
+    def check(self):
+        import select
+        if not self.conns:
+            return
+        readable, _, errored = select.select(self.conns, [], self.conns, 0)
+        for conn in set(readable) | set(errored):
+            try:
+                data = conn.recv(1, socket.MSG_PEEK)
+            except OSError:
+                data = b""
+            if not data:
+                raise RuntimeError(f"Rank {self.rank}: distributed peer closed its connection")
+
+    def close(self):
+        for conn in self.conns:
+            try:
+                conn.close()
+            except OSError:
+                pass
+        self.conns = []
+
+
+def rendezvous(rank: int, world_size: int, master_addr: str, timeout: float, make_id):
+    """Rank 0 calls make_id() and sends the bytes to every worker over TCP;
+    returns (id bytes, PeerLinks holding the open connections).
 
     Same topology and failure behaviour as the reference's _connect: rank 0
     binds and accepts world_size-1 peers within `timeout`; workers retry the
     connection until the deadline."""
     host, port = _parse_master_addr(master_addr)
     if world_size == 1:
-        return make_id()
+        return make_id(), PeerLinks(rank, [])
     if rank == 0:
         payload = make_id()
         if len(payload) != ID_BYTES:
@@ -107,12 +143,12 @@ def exchange_id(rank: int, world_size: int, master_addr: str, timeout: float, ma
                 for conn in peers:       # wait for every worker's acknowledgement
                     if _recv_exact(conn, 1) != b"\x01":
                         raise RuntimeError("bad acknowledgement from distributed peer")
-        except OSError as exc:
+        except (OSError, RuntimeError) as exc:
+            PeerLinks(rank, peers).close()
+            if isinstance(exc, RuntimeError):
+                raise
             raise RuntimeError(f"Rank 0 failed to initialize distributed listener at {master_addr}") from exc
-        finally:
-            for conn in peers:
-                conn.close()
-        return payload
+        return payload, PeerLinks(rank, peers)
     deadline = time.monotonic() + timeout
     last = None
     while time.monotonic() < deadline:
@@ -123,13 +159,19 @@ def exchange_id(rank: int, world_size: int, master_addr: str, timeout: float, ma
             cli.settimeout(max(0.001, deadline - time.monotonic()))
             payload = _recv_exact(cli, ID_BYTES)
             cli.sendall(b"\x01")
-            cli.close()
-            return payload
+            return payload, PeerLinks(rank, [cli])
         except (OSError, RuntimeError) as exc:
             last = exc
             cli.close()
             time.sleep(min(0.1, max(0.0, deadline - time.monotonic())))
     raise RuntimeError(f"Rank {rank} failed to connect to master at {master_addr}") from last
+
+
+def exchange_id(rank: int, world_size: int, master_addr: str, timeout: float, make_id) -> bytes:
+    """rendezvous() without the liveness channel: returns the id bytes."""
+    payload, links = rendezvous(rank, world_size, master_addr, timeout, make_id)
+    links.close()
+    return payload
 
 
 def nccl_unique_id() -> bytes:
@@ -198,23 +240,47 @@ class DistributedDataParallel:
         self.host, self.port = _parse_master_addr(master_addr)
         self.bucket_bytes = int(bucket_bytes)
         self.comm = None
+        self.links = None
 
     def _connect(self):
         if self.comm is not None or self.world_size <= 1:
             return
-        uid = exchange_id(self.rank, self.world_size, self.master_addr, self.timeout, nccl_unique_id)
+        uid, self.links = rendezvous(self.rank, self.world_size, self.master_addr, self.timeout,
+                                     nccl_unique_id)
         self.comm = NcclCommunicator(self.module.backend, self.rank, self.world_size, uid, self.timeout)
+        # A step waits on its peers through the gradient all-reduce; bound that
+        # wait by the same timeout the reference applies to its peer sockets.
+        self.module.backend.set_timeout(self.timeout)
         self.module.attach_comm(self.comm, self.bucket_bytes)
 
     def parameters(self):
         return self.module.get_parameters()
 
     def step(self, x, t) -> float:
+        """One data-parallel step.  A peer that stops taking part surfaces as
+        RuntimeError, as a lost peer socket does in the reference
+        (python/orca/distributed.py:65-80): one that left between steps is
+        seen on the rendezvous sockets before anything is launched; one that
+        stays but never joins makes the all-reduce miss the `timeout`
+        deadline.  The communicator is then aborted and this wrapper cannot
+        step again."""
         self._connect()
-        return self.module.step(x, t)
+        try:
+            if self.links is not None:
+                self.links.check()
+            return self.module.step(x, t)
+        except (RuntimeError, L.OrcaTimeout, L.OrcaCommError) as exc:
+            if self.comm is not None:
+                self.comm.abort()
+            if isinstance(exc, RuntimeError):
+                raise
+            raise RuntimeError(f"Rank {self.rank}: distributed peer stopped responding: {exc}") from exc
 
     def close(self):
         if self.comm is not None:
             self.module.attach_comm(None)
             self.comm.close()
             self.comm = None
+        if self.links is not None:
+            self.links.close()
+            self.links = None

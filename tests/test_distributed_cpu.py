@@ -6,7 +6,8 @@
 * argument validation raises the reference's TypeError/ValueError
   (distributed.py:19-62, python/tests/test_phase8.py:60-106);
 * a rank that never joins makes the others fail with RuntimeError after the
-  timeout instead of hanging;
+  timeout instead of hanging; a rank that leaves after joining is seen on
+  the kept rendezvous sockets before the next step;
 * the bench's plumbing over torch.distributed `gloo`, world 2: the id
   broadcast and the max-over-ranks timing reduction.
 """
@@ -52,6 +53,33 @@ def test_rendezvous_missing_peer_times_out():
         D.exchange_id(1, 2, addr, 1.0, lambda: bytes(128))   # nobody listens
     with pytest.raises(RuntimeError):
         D.exchange_id(0, 2, addr, 1.0, lambda: bytes(128))   # nobody connects
+
+
+def _leaver(addr, q):
+    payload, links = D.rendezvous(1, 2, addr, 20.0, lambda: bytes(128))
+    links.check()                     # rank 0 still there
+    q.put("joined")
+    links.close()                     # leave between steps
+
+
+def test_peer_links_report_a_rank_that_left():
+    """The rendezvous sockets stay open as the liveness channel: while the
+    worker is there check() passes; after it closes its end (or exits),
+    rank 0's next check() raises RuntimeError -- before any collective."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    addr = f"127.0.0.1:{_free_port()}"
+    p = ctx.Process(target=_leaver, args=(addr, q))
+    p.start()
+    payload, links = D.rendezvous(0, 2, addr, 20.0, lambda: bytes(range(128)))
+    assert payload == bytes(range(128))
+    links.check()
+    assert q.get(timeout=60) == "joined"
+    p.join(30)
+    assert p.exitcode == 0
+    with pytest.raises(RuntimeError, match="closed its connection"):
+        links.check()
+    links.close()
 
 
 @pytest.mark.parametrize("rank,world,exc", [(True, 2, TypeError), (0, "2", TypeError),
@@ -106,3 +134,12 @@ def test_bench_plumbing_gloo_world2():
     for r in range(2):
         assert res[r][0] == bytes([7] * 128)   # the NCCL id reaches every rank
         assert res[r][1] == 11.0               # max over ranks
+
+
+def test_allreduce_sweep_needs_two_ranks(capsys, monkeypatch):
+    """The sweep module loads without a GPU and declines a single rank."""
+    import json as _json
+    from orcaml_b200 import allreduce_sweep
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    assert allreduce_sweep.main([]) == 0
+    assert "skipped" in _json.loads(capsys.readouterr().out.strip().splitlines()[-1])

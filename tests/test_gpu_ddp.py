@@ -80,3 +80,77 @@ def test_ddp_two_gpus_matches_oracle(tmp_path, opt, dims, batch):
         assert np.array_equal(p0, p1)          # replicas stay identical
         err = float(np.linalg.norm(p0 - q) / np.linalg.norm(q))
         assert err <= 1e-4, (i, err)
+
+
+LEAVER = r'''
+import json, os, sys, time
+sys.path.insert(0, REPO)
+from orcaml_b200.backend import CudaBackend
+from orcaml_b200.mlp import MlpTrainer
+from orcaml_b200.distributed import DistributedDataParallel
+from orcaml_b200.synthetic import init_params, make_batch
+rank, port, mode = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3]
+dims, B = [784, 256, 256, 10], 64
+
+def wait_for(name, limit=120.0):
+    t0 = time.monotonic()
+    while not os.path.exists(os.path.join(OUT, name)):
+        if time.monotonic() - t0 > limit:
+            sys.exit(3)
+        time.sleep(0.05)
+
+be = CudaBackend(rank)
+tr = MlpTrainer(be, dims, B, optimizer="sgd", lr=0.01, momentum=0.9)
+tr.set_parameters(init_params(dims, 1))
+ddp = DistributedDataParallel(tr, rank=rank, world_size=2, master_addr=f"127.0.0.1:{port}",
+                              timeout=TIMEOUT)
+x, t, _ = make_batch(dims, B, rank)
+ddp.step(x, t)                                   # both ranks complete step 1
+if rank == 1:
+    if mode == "exit":
+        os._exit(0)                              # leaves between steps, nothing in flight
+    wait_for("rank0.done")                       # alive but never joins step 2
+    ddp.comm.abort()
+    sys.exit(0)
+if mode == "exit":
+    wait_for("rank1.exited")
+t0 = time.monotonic()
+try:
+    ddp.step(x, t)
+    res = {"raised": None}
+except RuntimeError as e:
+    res = {"raised": str(e)}
+res["elapsed"] = time.monotonic() - t0
+json.dump(res, open(os.path.join(OUT, "rank0.json"), "w"))
+open(os.path.join(OUT, "rank0.done"), "w").close()
+ddp.close()
+tr.close()
+be.close()
+'''
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_ddp_peer_loss_raises_instead_of_hanging(tmp_path, mode):
+    """A peer that exits between steps is seen on the rendezvous sockets before
+    the next step launches anything ("exit"); a peer that stays but never joins
+    the next step makes the all-reduce miss the 10 s deadline, the
+    communicator is aborted ("stall").  Either way the surviving rank gets
+    RuntimeError, well before any outer bound, and exits cleanly.  NVLS is off
+    (NCCL_NVLS_ENABLE=0) so no rank's memory is bound to a multicast object."""
+    port = 29611 + (0 if mode == "exit" else 7)
+    code = f"REPO = {REPO!r}\nOUT = {str(tmp_path)!r}\nTIMEOUT = 10.0\n" + LEAVER
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, "-c", code, str(r), str(port), mode], env=env)
+             for r in range(2)]
+    if mode == "exit":
+        assert procs[1].wait(timeout=300) == 0
+        (tmp_path / "rank1.exited").touch()
+    assert procs[0].wait(timeout=300) == 0
+    assert procs[1].wait(timeout=300) == 0
+    res = json.load(open(tmp_path / "rank0.json"))
+    assert res["raised"] is not None
+    if mode == "exit":
+        assert "closed its connection" in res["raised"] and res["elapsed"] < 5.0
+    else:
+        assert "stopped responding" in res["raised"] and 9.0 <= res["elapsed"] < 60.0
