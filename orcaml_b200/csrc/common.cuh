@@ -83,6 +83,11 @@ void ctx_release(orca_ctx* ctx);
 // context's deadline.
 orca_status sync_stream(orca_ctx* ctx);
 orca_status sync_stream_for(orca_ctx* ctx, cudaStream_t stream, double timeout_s);
+// Device -> (pageable) host copy after the compute stream.  A copy into
+// pageable memory blocks the calling thread until the stream reaches it, with
+// no bound, so the stream is first drained with the deadline: a stream that
+// never drains gives ORCA_TIMEOUT instead of a thread stuck in the copy.
+orca_status copy_to_host(orca_ctx* ctx, void* dst, const void* src, size_t bytes);
 // Reads and clears the device error word (synchronises the compute stream).
 orca_status check_device_error(orca_ctx* ctx);
 inline void count_launch(orca_ctx* ctx, uint64_t n = 1) { ctx->launches += n; }

@@ -289,6 +289,9 @@ constexpr int A_STAGE = 2 * A_PLANE;                 // hi + lo
 constexpr int B_STAGE = 2 * B_PLANE;
 constexpr int TILE_BYTES = STAGES * (A_STAGE + B_STAGE);   // 192 KB
 constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
+// With the next-layer dot: one (HEAD_MAX_CLASSES + 1)-float slot per
+// epilogue thread, right after the 256 bytes of barriers.
+constexpr int SMEM_BYTES_DOT = SMEM_BYTES + 32 * 8 * (16 + 1) * 4;
 constexpr int EPI_WARPS = 8;                         // 2 per TMEM lane quarter, 128 columns each
 constexpr int THREADS = 64 + 32 * EPI_WARPS;         // producer + MMA + epilogue warps
 constexpr int TMEM_COLS = 2 * BN;                    // two accumulator buffers
@@ -369,19 +372,41 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* ma
   }
 }
 
+// part[j] += a * W[n, j] for the next-layer dot (W read as hi + lo; every
+// lane of a warp reads the same column n, so the loads are broadcasts).  part
+// is the thread's own slot in shared memory: the epilogue's 128 accumulators
+// leave no registers for it.  volatile keeps each update a shared-memory
+// access instead of letting the compiler hold the sums in registers.
+__device__ __forceinline__ void dot_accum(const Epilogue& ep, int64_t n, float a,
+                                          volatile float* part) {
+  const float* wh = ep.dot_hi + n * ep.dot_ld;
+  const float* wl = ep.dot_lo + n * ep.dot_ld;
+  for (int j = 0; j < ep.dot_n; ++j)
+    part[j] = fmaf(a, __fadd_rn(__ldg(wh + j), __ldg(wl + j)), part[j]);
+}
+
 // Stores columns [n0, n0+32) of row m from acc[Q*32 .. Q*32+32) through the
-// epilogue.  Q is a template parameter so that every accumulator index is a
-// compile-time constant and the array stays in registers.
-template <int Q>
+// epilogue (and, with kDot, adds their next-layer dot into part).  Q is a
+// template parameter so that every accumulator index is a compile-time
+// constant and the array stays in registers.
+template <int Q, bool kDot>
 __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, int64_t N, int64_t m,
-                                               int64_t n0, const float (&acc)[128]) {
+                                               int64_t n0, const float (&acc)[128],
+                                               volatile float* part) {
 #define v(i) acc[Q * 32 + (i)]
   if (m >= M) return;
   const bool full = (n0 + 32 <= N) && ((ep.ldc & 3) == 0);
   if (!full) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (n0 + j < N) store_epi(ep, m, n0 + j, v(j));
+    for (int j = 0; j < 32; ++j) {
+      if (n0 + j < N) {
+        store_epi(ep, m, n0 + j, v(j));
+        if (kDot) {
+          const float y = __fadd_rn(v(j), ep.bias[n0 + j]);
+          dot_accum(ep, n0 + j, y > 0.0f ? y : 0.0f, part);
+        }
+      }
+    }
     return;
   }
   const int64_t base = m * ep.ldc + n0;
@@ -413,6 +438,7 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
       for (int e = 0; e < 4; ++e) {
         float y = __fadd_rn(x[e], ep.bias[n0 + 4 * q + e]);
         x[e] = y > 0.0f ? y : 0.0f;
+        if (kDot) dot_accum(ep, n0 + 4 * q + e, x[e], part);
       }
     } else if (ep.mode == EPI_MASK_SPLIT) {
       float4 a = mh[q], b = ml[q];
@@ -432,6 +458,7 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
 }
 #undef v
 
+template <bool kDot>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const Params p) {
@@ -605,10 +632,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       if (!ok) break;
       const int64_t m = tm * BM + quarter * 32 + lane;
       const int64_t nb = tn * BN + half * 128;
-      if (nb < p.N) epilogue_chunk<0>(p.ep, p.M, p.N, m, nb, acc);
-      if (nb + 32 < p.N) epilogue_chunk<1>(p.ep, p.M, p.N, m, nb + 32, acc);
-      if (nb + 64 < p.N) epilogue_chunk<2>(p.ep, p.M, p.N, m, nb + 64, acc);
-      if (nb + 96 < p.N) epilogue_chunk<3>(p.ep, p.M, p.N, m, nb + 96, acc);
+      // Dot slot of this epilogue thread: 17 floats apart (conflict-free).
+      volatile float* part = reinterpret_cast<volatile float*>(smem + TILE_BYTES + 256) +
+                             (threadIdx.x - 64) * (HEAD_MAX_CLASSES + 1);
+      if (kDot)
+        for (int j = 0; j < HEAD_MAX_CLASSES; ++j) part[j] = 0.0f;
+      if (nb < p.N) epilogue_chunk<0, kDot>(p.ep, p.M, p.N, m, nb, acc, part);
+      if (nb + 32 < p.N) epilogue_chunk<1, kDot>(p.ep, p.M, p.N, m, nb + 32, acc, part);
+      if (nb + 64 < p.N) epilogue_chunk<2, kDot>(p.ep, p.M, p.N, m, nb + 64, acc, part);
+      if (nb + 96 < p.N) epilogue_chunk<3, kDot>(p.ep, p.M, p.N, m, nb + 96, acc, part);
+      if (kDot && m < p.M && nb < p.N) {
+        // BN is a multiple of DOT_SLICE: nb / DOT_SLICE is this half-tile's slice.
+        float* o = p.ep.dot_out + ((nb / DOT_SLICE) * p.M + m) * p.ep.dot_ldp;
+        for (int j = 0; j < p.ep.dot_n; ++j) o[j] = part[j];
+      }
     }
   }
 
@@ -665,7 +702,10 @@ bool eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const Operand& 
   if (M < 64 || N < 64 || K < BK) return false;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
   if (!operand_ok(A) || !operand_ok(B)) return false;
-  (void)ep;
+  if (ep.dot_out && (ep.mode != EPI_BIAS_RELU_SPLIT || ep.dot_n < 1 ||
+                     ep.dot_n > HEAD_MAX_CLASSES || ep.dot_ldp < ep.dot_n || !ep.dot_hi ||
+                     !ep.dot_lo || ep.dot_ld < ep.dot_n))
+    return false;
   return true;
 }
 
@@ -685,8 +725,11 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
                    const Operand& B, const Epilogue& ep) {
   static bool attr_set[64] = {};
   if (ctx->device < 64 && !attr_set[ctx->device]) {
-    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES));
+    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES_DOT));
     attr_set[ctx->device] = true;
   }
   CUtensorMap ma, mb;
@@ -711,12 +754,150 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
   p.chunk_kb = (int)std::max<int64_t>(1, std::min<int64_t>(nk, want));
   const int64_t tiles = cdiv(M, BM) * cdiv(N, BN);
   const int grid = (int)std::min<int64_t>(tiles, ctx->sm_count);
-  tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
+  static_assert(BN % DOT_SLICE == 0 && DOT_SLICE == 128, "one dot slice per epilogue half");
+  static_assert(EPI_WARPS == 8 && HEAD_MAX_CLASSES == 16 && SMEM_BYTES_DOT <= 232448,
+                "dot slots: 256 epilogue threads x 17 floats");
+  if (ep.dot_out) tc_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES_DOT, ctx->stream>>>(ma, mb, p);
+  else tc_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
   count_launch(ctx);
   ORCA_CUDA_TRY(cudaGetLastError());
   return ORCA_OK;
 }
 }  // namespace tc
+
+// =============================================================== classifier head
+// The classifier layer (C <= 16 outputs) is memory-bound: its three products
+// (logits, dW, dX) each stream the [B, H] activation planes once in the plain
+// GEMM formulation.  Here the logits come from the previous GEMM's epilogue
+// (the next-layer dot) and are only reduced over column slices; dW and dX
+// share one pass over the activation.
+namespace head {
+constexpr int THREADS = 256;
+constexpr int ROW_CHUNK = 256;        // rows of g staged in shared memory at a time
+constexpr int MAX_ROW_BLOCKS = 64;
+
+__global__ void __launch_bounds__(256)
+logits_kernel(const float* __restrict__ part, int64_t slices, int64_t M, int C, int64_t ldp,
+              const float* __restrict__ bias, float* __restrict__ logits) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * C) return;
+  const int64_t m = i / C;
+  const int j = (int)(i % C);
+  float s = 0.0f;
+  for (int64_t sl = 0; sl < slices; ++sl) s = __fadd_rn(s, part[(sl * M + m) * ldp + j]);
+  logits[i] = __fadd_rn(s, bias[j]);
+}
+
+// Thread per activation column n; a block covers 256 columns and one block of
+// rows, walking it in order.  Per row: one masked dot over the C classes
+// (dX, same FMA order as the plain product) and C FMAs into the column's dW
+// partial.
+__global__ void __launch_bounds__(THREADS)
+bwd_kernel(int64_t B, int64_t H, int C, int64_t rows, const float* __restrict__ g,
+           const float* __restrict__ a_hi, const float* __restrict__ a_lo,
+           const float* __restrict__ w_hi, const float* __restrict__ w_lo,
+           float* __restrict__ dz_hi, float* __restrict__ dz_lo, float* __restrict__ part) {
+  __shared__ float gs[ROW_CHUNK * HEAD_MAX_CLASSES];
+  const int64_t n = (int64_t)blockIdx.x * THREADS + threadIdx.x;
+  const int64_t m_begin = (int64_t)blockIdx.y * rows;
+  const int64_t m_end = std::min<int64_t>(B, m_begin + rows);
+  const bool active = n < H;
+  float w[HEAD_MAX_CLASSES], dw[HEAD_MAX_CLASSES];
+#pragma unroll
+  for (int j = 0; j < HEAD_MAX_CLASSES; ++j) {
+    w[j] = (active && j < C) ? __fadd_rn(w_hi[n * C + j], w_lo[n * C + j]) : 0.0f;
+    dw[j] = 0.0f;
+  }
+  for (int64_t c0 = m_begin; c0 < m_end; c0 += ROW_CHUNK) {
+    const int nr = (int)std::min<int64_t>(ROW_CHUNK, m_end - c0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < nr * HEAD_MAX_CLASSES; e += THREADS) {
+      const int r = e / HEAD_MAX_CLASSES, j = e % HEAD_MAX_CLASSES;
+      gs[e] = j < C ? g[(c0 + r) * C + j] : 0.0f;
+    }
+    __syncthreads();
+    if (!active) continue;
+    int r = 0;
+    for (; r < nr; r += 4) {
+      const int cnt = std::min(4, nr - r);
+      float a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t idx = (c0 + r + u) * H + n;
+        a[u] = u < cnt ? __fadd_rn(a_hi[idx], a_lo[idx]) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (u >= cnt) break;
+        const float* gr = gs + (r + u) * HEAD_MAX_CLASSES;
+        float d = 0.0f;
+#pragma unroll
+        for (int j = 0; j < HEAD_MAX_CLASSES; ++j)
+          if (j < C) d = fmaf(gr[j], w[j], d);
+        const float gv = a[u] > 0.0f ? d : 0.0f;
+        float h, l;
+        split_tf32(gv, h, l);
+        const int64_t idx = (c0 + r + u) * H + n;
+        dz_hi[idx] = h;
+        dz_lo[idx] = l;
+#pragma unroll
+        for (int j = 0; j < HEAD_MAX_CLASSES; ++j)
+          if (j < C) dw[j] = fmaf(a[u], gr[j], dw[j]);
+      }
+    }
+  }
+  if (!active) return;
+#pragma unroll
+  for (int j = 0; j < HEAD_MAX_CLASSES; ++j)
+    if (j < C) part[((int64_t)blockIdx.y * C + j) * H + n] = dw[j];
+}
+
+__global__ void __launch_bounds__(256)
+dw_reduce_kernel(int64_t H, int C, int64_t row_blocks, const float* __restrict__ part,
+                 float* __restrict__ dw) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= H * C) return;
+  const int64_t n = i % H;
+  const int j = (int)(i / H);
+  float s = 0.0f;
+  for (int64_t rb = 0; rb < row_blocks; ++rb) s = __fadd_rn(s, part[(rb * C + j) * H + n]);
+  dw[n * C + j] = s;
+}
+}  // namespace head
+
+orca_status head_logits(orca_ctx* ctx, const float* part, int64_t slices, int64_t M, int C,
+                        int64_t ldp, const float* bias, float* logits) {
+  if (C < 1 || C > HEAD_MAX_CLASSES || ldp < C || slices < 1)
+    return fail(ORCA_INVALID_ARGUMENT, "head_logits: bad shape");
+  if (M <= 0) return ORCA_OK;
+  head::logits_kernel<<<(unsigned)cdiv(M * C, 256), 256, 0, ctx->stream>>>(part, slices, M, C,
+                                                                            ldp, bias, logits);
+  count_launch(ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+int64_t head_row_blocks(int64_t B) {
+  return std::max<int64_t>(1, std::min<int64_t>(head::MAX_ROW_BLOCKS, cdiv(B, head::ROW_CHUNK)));
+}
+
+int64_t head_part_floats(int64_t B, int64_t H, int C) { return head_row_blocks(B) * C * H; }
+
+orca_status head_backward(orca_ctx* ctx, int64_t B, int64_t H, int C, const float* g,
+                          const float* act_hi, const float* act_lo, const float* w_hi,
+                          const float* w_lo, float* dz_hi, float* dz_lo, float* part, float* dw) {
+  if (C < 1 || C > HEAD_MAX_CLASSES) return fail(ORCA_INVALID_ARGUMENT, "head_backward: C");
+  if (B <= 0 || H <= 0) return ORCA_OK;
+  const int64_t rb = head_row_blocks(B);
+  const int64_t rows = cdiv(B, rb);
+  dim3 grid((unsigned)cdiv(H, head::THREADS), (unsigned)rb);
+  head::bwd_kernel<<<grid, head::THREADS, 0, ctx->stream>>>(B, H, C, rows, g, act_hi, act_lo, w_hi,
+                                                            w_lo, dz_hi, dz_lo, part);
+  head::dw_reduce_kernel<<<(unsigned)cdiv(H * C, 256), 256, 0, ctx->stream>>>(H, C, rb, part, dw);
+  count_launch(ctx, 2);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
 
 // =============================================================== dispatch
 // GEMM_AUTO takes the tensor-core kernel when the operands allow it and the
@@ -746,6 +927,8 @@ orca_status gemm(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& 
                  size_t workspace_bytes) {
   if (M <= 0 || N <= 0) return ORCA_OK;
   if (use_tc(ctx, M, N, K, A, B, ep, path)) return tc::launch(ctx, M, N, K, A, B, ep);
+  if (ep.dot_out)
+    return fail(ORCA_INVALID_ARGUMENT, "gemm: the next-layer dot needs the tensor-core path");
 
   if (N <= skinny::NMAX && K > 0) {
     // K-major A: a warp per row reads its row contiguously.  MN-major A (the

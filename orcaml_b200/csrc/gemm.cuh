@@ -35,7 +35,22 @@ struct Epilogue {
   const float* bias = nullptr;
   const float* mask_hi = nullptr;   // same [M, ldc] layout as out
   const float* mask_lo = nullptr;
+  // Next-layer dot (EPI_BIAS_RELU_SPLIT on the tensor-core path only): the
+  // activation a[m, n] also feeds the classifier layer's product.  Slice s of
+  // 128 output columns writes, for j < dot_n (<= 16),
+  //   dot_out[(s * M + m) * dot_ldp + j] = sum_{n in slice} a[m, n] * W[n, j]
+  // with W[n, j] = dot_hi[n * dot_ld + j] + dot_lo[...] (sequential FMA over n).
+  const float* dot_hi = nullptr;
+  const float* dot_lo = nullptr;
+  int64_t dot_ld = 0;
+  int dot_n = 0;
+  float* dot_out = nullptr;
+  int64_t dot_ldp = 0;
 };
+
+// Columns of the activation covered by one dot_out slice.
+constexpr int DOT_SLICE = 128;
+constexpr int HEAD_MAX_CLASSES = 16;
 
 // AUTO: tensor cores when eligible and large enough; SIMT: FFMA kernels only;
 // TC: tensor cores whenever eligible (skinny/unaligned shapes still use SIMT).
@@ -53,6 +68,22 @@ bool gemm_tc_eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const O
 // Which path `gemm` would take (for reporting and tests).
 int gemm_select(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
                 const Operand& B, const Epilogue& ep, int path);
+
+// Classifier layer with C <= HEAD_MAX_CLASSES outputs.
+// head_logits: logits[m, j] = (sum over s of part[(s*M + m)*ldp + j]) + bias[j],
+// the slices summed in order -- the reduction of the next-layer dot above.
+orca_status head_logits(orca_ctx* ctx, const float* part, int64_t slices, int64_t M, int C,
+                        int64_t ldp, const float* bias, float* logits);
+// head_backward: from g = dlogits [B, C] (plain fp32), the layer input
+// act = (act_hi + act_lo) [B, H] and W = (w_hi + w_lo) [H, C], in one pass
+// over act: dZ[m, n] = act > 0 ? sum_j g[m, j] W[n, j] : 0 written as planes,
+// and dW[n, j] = sum_m act[m, n] g[m, j] (row blocks summed in order through
+// `part`, which needs head_part_floats(B, H, C) floats).
+int64_t head_row_blocks(int64_t B);
+int64_t head_part_floats(int64_t B, int64_t H, int C);
+orca_status head_backward(orca_ctx* ctx, int64_t B, int64_t H, int C, const float* g,
+                          const float* act_hi, const float* act_lo, const float* w_hi,
+                          const float* w_lo, float* dz_hi, float* dz_lo, float* part, float* dw);
 
 // Split a plain fp32 array into (hi, lo) planes: n elements.
 orca_status split_planes(orca_ctx* ctx, const float* x, float* hi, float* lo, int64_t n);

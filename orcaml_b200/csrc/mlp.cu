@@ -271,6 +271,13 @@ struct orca_mlp {
   float* dz[2] = {nullptr, nullptr}; // ping-pong (hi, lo) planes of hidden-layer dZ
   int64_t dz_plane = 0;              // elements per plane in dz buffers
   float* colsum_part = nullptr;
+  // Classifier-layer fusion (C <= HEAD_MAX_CLASSES, at least one hidden
+  // layer, tensor-core path allowed): logits from the last hidden GEMM's
+  // epilogue, dW and dX of the classifier layer in one pass (head_* kernels).
+  bool use_head = false;
+  float* host_stage = nullptr;       // pinned: [0] loss, [1] device error word
+  float* head_part = nullptr;        // dot slices [S][B][head_ldp] or dW row-block partials
+  int64_t head_ldp = 0;
   float* workspace = nullptr;
   size_t workspace_bytes = 0;
   std::vector<void*> allocs;
@@ -459,6 +466,16 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
   ALLOC(colsum_part, (size_t)(cdiv(B, COLSUM_ROWS) * maxn) * 4);
   m->workspace_bytes = (size_t)64 * (size_t)maxn * 16 * 4;
   ALLOC(workspace, m->workspace_bytes);
+  if (cudaMallocHost(reinterpret_cast<void**>(&m->host_stage), 2 * sizeof(float)) != cudaSuccess)
+    return cleanup(fail(ORCA_CUDA_ERROR, "pinned host allocation failed"));
+  m->use_head = L >= 2 && C <= HEAD_MAX_CLASSES && m->gemm_path != GEMM_SIMT;
+  if (m->use_head) {
+    const int64_t H = m->dims[L - 1];
+    m->head_ldp = (C + 3) / 4 * 4;
+    const int64_t fwd = cdiv(H, DOT_SLICE) * B * m->head_ldp;
+    const int64_t bwd = head_part_floats(B, H, (int)C);
+    ALLOC(head_part, (size_t)std::max(fwd, bwd) * 4);
+  }
 #undef ALLOC
   for (int l = 0; l < 64; ++l) m->ev_layer[l] = nullptr;
   for (int l = 0; l < L; ++l)
@@ -477,6 +494,7 @@ orca_status orca_mlp_destroy(orca_mlp* m) {
   sync_stream_for(m->ctx, m->ctx->stream, m->ctx->sync_timeout_s);
   sync_stream_for(m->ctx, m->ctx->comm_stream, m->ctx->sync_timeout_s);
   for (void* p : m->allocs) cudaFree(p);
+  if (m->host_stage) cudaFreeHost(m->host_stage);
   for (int l = 0; l < 64; ++l)
     if (m->ev_layer[l]) cudaEventDestroy(m->ev_layer[l]);
   if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
@@ -537,13 +555,14 @@ orca_status orca_mlp_get_param(orca_mlp* m, int index, float* host, int64_t nume
     merge_planes_kernel<<<ew_grid(m->ctx, n), 256, 0, m->ctx->stream>>>(m->w_hi[l], m->w_lo[l],
                                                                         tmp, n);
     count_launch(m->ctx);
-    ORCA_CUDA_TRY(cudaMemcpyAsync(host, tmp, (size_t)n * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+    orca_status st = finish_sync(m);
+    if (st == ORCA_OK) st = copy_to_host(m->ctx, host, tmp, (size_t)n * 4);
     cudaFreeAsync(tmp, m->ctx->stream);
+    ORCA_TRY(st);
   } else {
-    ORCA_CUDA_TRY(cudaMemcpyAsync(host, m->bias[l], (size_t)n * 4, cudaMemcpyDeviceToHost,
-                                  m->ctx->stream));
+    ORCA_TRY(finish_sync(m));
+    ORCA_TRY(copy_to_host(m->ctx, host, m->bias[l], (size_t)n * 4));
   }
-  ORCA_TRY(finish_sync(m));
   return check_device_error(m->ctx);
 }
 
@@ -553,9 +572,8 @@ orca_status orca_mlp_get_grad(orca_mlp* m, int index, float* host, int64_t numel
   if (n != numel || !host) return fail(ORCA_SHAPE_MISMATCH, "get_grad: size");
   ORCA_TRY(check_ctx(m->ctx));
   std::lock_guard<std::mutex> lk(m->ctx->mu);
-  ORCA_CUDA_TRY(cudaMemcpyAsync(host, m->grads + m->p_off[index], (size_t)n * 4,
-                                cudaMemcpyDeviceToHost, m->ctx->stream));
   ORCA_TRY(finish_sync(m));
+  ORCA_TRY(copy_to_host(m->ctx, host, m->grads + m->p_off[index], (size_t)n * 4));
   return check_device_error(m->ctx);
 }
 
@@ -606,9 +624,17 @@ orca_status orca_mlp_step(orca_mlp* m, const float* x, const float* t, float* lo
                                 ctx->stream));
   ORCA_TRY(step_device_locked(m, m->x_stage, m->t_buf, nullptr));
   if (loss) {
-    ORCA_CUDA_TRY(cudaMemcpyAsync(loss, m->loss, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    // Loss and the device error word come back through pinned memory (the
+    // copies do not block), then one bounded wait covers the whole step.
+    ORCA_CUDA_TRY(cudaMemcpyAsync(&m->host_stage[0], m->loss, 4, cudaMemcpyDeviceToHost,
+                                  ctx->stream));
+    ORCA_CUDA_TRY(cudaMemcpyAsync(&m->host_stage[1], ctx->dev_err, 4, cudaMemcpyDeviceToHost,
+                                  ctx->stream));
     ORCA_TRY(finish_sync(m));
-    return check_device_error(ctx);
+    *loss = m->host_stage[0];
+    int h;
+    memcpy(&h, &m->host_stage[1], sizeof(int));
+    if (h != DEV_OK) return check_device_error(ctx);   // clears the word, maps the code
   }
   return ORCA_OK;
 }
@@ -636,12 +662,9 @@ orca_status orca_mlp_forward(orca_mlp* m, const float* x, const float* t, float*
     ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(m->row_loss, B, 1.0f / (float)B, m->loss);
     count_launch(ctx, 2);
   }
-  if (logits)
-    ORCA_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)(B * C) * 4, cudaMemcpyDeviceToHost,
-                                  ctx->stream));
-  if (loss && t)
-    ORCA_CUDA_TRY(cudaMemcpyAsync(loss, m->loss, 4, cudaMemcpyDeviceToHost, ctx->stream));
   ORCA_TRY(finish_sync(m));
+  if (logits) ORCA_TRY(copy_to_host(ctx, logits, m->logits, (size_t)(B * C) * 4));
+  if (loss && t) ORCA_TRY(copy_to_host(ctx, loss, m->loss, 4));
   return check_device_error(ctx);
 }
 
@@ -724,11 +747,35 @@ static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad) {
       ep.out = m->logits;
       ep.ldc = N;
     }
+    bool fused_head = false;
+    if (m->use_head && l == L - 2) {
+      // The classifier layer's product rides on this GEMM's epilogue when it
+      // takes the tensor cores.
+      Epilogue ed = ep;
+      ed.dot_hi = m->w_hi[L - 1];
+      ed.dot_lo = m->w_lo[L - 1];
+      ed.dot_ld = C;
+      ed.dot_n = (int)C;
+      ed.dot_out = m->head_part;
+      ed.dot_ldp = m->head_ldp;
+      if (gemm_select(ctx, B, N, K, a, w, ed, m->gemm_path) == GEMM_TC) {
+        ep = ed;
+        fused_head = true;
+      }
+    }
     const int path = gemm_select(ctx, B, N, K, a, w, ep, m->gemm_path);
     const int pr = prof_open(m, "gemm_fwd_l" + std::to_string(l), 2.0 * B * N * K,
                              4.0 * (2 * B * K + 2 * K * N + (l + 1 < L ? 2 : 1) * B * N), path);
     ORCA_TRY(gemm(ctx, B, N, K, a, w, ep, m->gemm_path, m->workspace, m->workspace_bytes));
     prof_close(m, pr);
+    if (fused_head) {
+      const int ph = prof_open(m, "head_logits", 2.0 * B * N * C,
+                               4.0 * (cdiv(N, DOT_SLICE) * B * m->head_ldp + B * C + C));
+      ORCA_TRY(head_logits(ctx, m->head_part, cdiv(N, DOT_SLICE), B, (int)C, m->head_ldp,
+                           m->bias[L - 1], m->logits));
+      prof_close(m, ph);
+      break;   // the classifier layer is done
+    }
   }
   if (with_loss_grad) {
     const int pr = prof_open(m, "softmax_ce", 0.0, 4.0 * (3 * B * C + B));
@@ -774,6 +821,21 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
                        4.0 * ((g_lo ? 2 : 1) * B * N + N));
     ORCA_TRY(colsum(ctx, g_hi, g_lo, B, N, g_ld, m->grads + m->p_off[2 * l + 1], m->colsum_part));
     prof_close(m, pr);
+    if (m->use_head && l == L - 1) {
+      // dW and dX of the classifier layer in one pass over its input.
+      pr = prof_open(m, "head_bwd_l" + std::to_string(l), 4.0 * B * N * K,
+                     4.0 * (2 * B * K + B * N + 2 * K * N + 2 * B * K + K * N));
+      ORCA_TRY(head_backward(ctx, B, K, (int)N, g_hi, m->act_planes[l], m->act_planes[l] + B * K,
+                             m->w_hi[l], m->w_lo[l], m->dz[cur], m->dz[cur] + B * K,
+                             m->head_part, m->grads + m->p_off[2 * l]));
+      prof_close(m, pr);
+      if (m->comm) ORCA_TRY(launch_layer_allreduce(m, l));
+      g_hi = m->dz[cur];
+      g_lo = m->dz[cur] + B * K;
+      g_ld = K;
+      cur ^= 1;
+      continue;
+    }
     // dW = act^T @ g : M = K (features), N, K_gemm = B.
     Operand at, g;
     at.hi = l == 0 ? m->x_planes : m->act_planes[l];

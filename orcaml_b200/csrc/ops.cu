@@ -111,10 +111,16 @@ orca_status sync_stream_for(orca_ctx* ctx, cudaStream_t stream, double timeout_s
   }
 }
 
+orca_status copy_to_host(orca_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  ORCA_TRY(sync_stream(ctx));
+  if (!bytes) return ORCA_OK;
+  ORCA_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  return sync_stream(ctx);
+}
+
 orca_status check_device_error(orca_ctx* ctx) {
   int h = 0;
-  ORCA_CUDA_TRY(cudaMemcpyAsync(&h, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
-  ORCA_TRY(sync_stream(ctx));
+  ORCA_TRY(copy_to_host(ctx, &h, ctx->dev_err, sizeof(int)));
   if (h != DEV_OK) {
     ORCA_CUDA_TRY(cudaMemsetAsync(ctx->dev_err, 0, sizeof(int), ctx->stream));
     if (h == DEV_WAIT_TIMEOUT)
@@ -510,9 +516,7 @@ orca_status orca_to_f32_vec(orca_ctx* ctx, const orca_buf* buf, float* dst, size
   if (buf->dtype != ORCA_F32) return fail(ORCA_DTYPE_MISMATCH, "to_f32_vec on a non-F32 buffer");
   if (n_elems != buf->n)
     return fail(ORCA_SHAPE_MISMATCH, "to_f32_vec: buffer has %zu elements, dst %zu", buf->n, n_elems);
-  if (n_elems)
-    ORCA_CUDA_TRY(cudaMemcpyAsync(dst, buf->ptr, n_elems * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  ORCA_TRY(sync_stream(ctx));
+  ORCA_TRY(copy_to_host(ctx, dst, buf->ptr, n_elems * 4));
   return check_device_error(ctx);
 }
 
@@ -540,9 +544,7 @@ orca_status orca_to_bytes(orca_ctx* ctx, const orca_buf* buf, void* dst, size_t 
   if (!buf) return fail(ORCA_INVALID_ARGUMENT, "null buffer");
   if (n_bytes != buf->n * dtype_size(buf->dtype))
     return fail(ORCA_SHAPE_MISMATCH, "to_bytes: size mismatch");
-  if (n_bytes)
-    ORCA_CUDA_TRY(cudaMemcpyAsync(dst, buf->ptr, n_bytes, cudaMemcpyDeviceToHost, ctx->stream));
-  ORCA_TRY(sync_stream(ctx));
+  ORCA_TRY(copy_to_host(ctx, dst, buf->ptr, n_bytes));
   return check_device_error(ctx);
 }
 
@@ -970,9 +972,9 @@ orca_status orca_has_nan_or_inf(orca_ctx* ctx, const orca_buf* x, orca_dtype dty
     count_launch(ctx);
   }
   int h = 0;
-  ORCA_CUDA_TRY(cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+  const orca_status st = copy_to_host(ctx, &h, flag, sizeof(int));
   cudaFreeAsync(flag, ctx->stream);
-  ORCA_TRY(sync_stream(ctx));
+  ORCA_TRY(st);
   *result = h;
   return ORCA_OK;
 }

@@ -63,8 +63,14 @@ def test_ddp_two_gpus_matches_oracle(tmp_path, opt, dims, batch):
     procs = [subprocess.Popen([sys.executable, "-c", code, str(r), str(world), str(port),
                                json.dumps(dims), str(batch), str(steps), opt])
              for r in range(world)]
-    for p in procs:
-        assert p.wait(timeout=600) == 0
+    try:
+        for p in procs:
+            assert p.wait(timeout=600) == 0
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+                p.wait(timeout=60)
     kw = dict(lr=1e-3, weight_decay=0.01) if opt == "adamw" else dict(lr=0.01, momentum=0.9)
     ref = O.OracleTrainer(dims, init_params(dims, 1), optimizer=opt, **kw)
     batches = [make_batch(dims, batch, r) for r in range(world)]
@@ -143,11 +149,17 @@ def test_ddp_peer_loss_raises_instead_of_hanging(tmp_path, mode):
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     procs = [subprocess.Popen([sys.executable, "-c", code, str(r), str(port), mode], env=env)
              for r in range(2)]
-    if mode == "exit":
-        assert procs[1].wait(timeout=300) == 0
-        (tmp_path / "rank1.exited").touch()
-    assert procs[0].wait(timeout=300) == 0
-    assert procs[1].wait(timeout=300) == 0
+    try:
+        if mode == "exit":
+            assert procs[1].wait(timeout=120) == 0
+            (tmp_path / "rank1.exited").touch()
+        assert procs[0].wait(timeout=120) == 0
+        assert procs[1].wait(timeout=120) == 0
+    finally:
+        for p in procs:          # never leave a rank behind holding a GPU
+            if p.poll() is None:
+                p.kill()
+                p.wait(timeout=60)
     res = json.load(open(tmp_path / "rank0.json"))
     assert res["raised"] is not None
     if mode == "exit":

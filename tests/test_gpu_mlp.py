@@ -115,6 +115,28 @@ def test_first_step_gradients_match_oracle(be):
     tr.close()
 
 
+@pytest.mark.parametrize("dims,B", [([784, 300, 200, 7], 200), ([64, 136, 1000, 16], 96),
+                                    ([784, 512, 256, 10], 256), ([32, 64, 64, 17], 64)])
+def test_classifier_head_fusion(be, dims, B):
+    """The classifier layer (C <= 16) on the tensor-core path: logits from the
+    last hidden GEMM's epilogue (ragged 128-column slices, C not a multiple of
+    4, C = 16) and dW/dX in one pass; C = 17 takes the plain products.  Loss,
+    logits and every gradient of one step against the oracle."""
+    x, t, _ = make_batch(dims, B, 5)
+    tr = make(be, dims, B, "sgd", "tc", lr=0.0)
+    logits, loss = tr.forward(x, t)
+    ref_loss, ref_logits = O.mlp_forward(dims, init_params(dims, 1), x, t)
+    scale = np.abs(ref_logits).max()
+    assert np.abs(logits - ref_logits).max() <= 1e-5 * scale
+    assert abs(loss - ref_loss) <= 1e-6 * abs(ref_loss)
+    lg = tr.step(x, t)
+    loss_ref, grads_ref, _ = O.mlp_forward_backward(dims, init_params(dims, 1), x, t)
+    assert abs(lg - loss_ref) <= 1e-6 * abs(loss_ref)
+    for i, (g, r) in enumerate(zip(tr.get_grads(), grads_ref)):
+        assert rel_err(g, r) <= 1e-5, (i, rel_err(g, r))
+    tr.close()
+
+
 @pytest.mark.parametrize("name", ["sgdm_small", "sgd_small"])
 def test_golden_small_cases(be, golden, name):
     """Goldens made from the reference's Python frontend (tests/golden)."""
