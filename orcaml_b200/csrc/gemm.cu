@@ -289,9 +289,12 @@ constexpr int A_STAGE = 2 * A_PLANE;                 // hi + lo
 constexpr int B_STAGE = 2 * B_PLANE;
 constexpr int TILE_BYTES = STAGES * (A_STAGE + B_STAGE);   // 192 KB
 constexpr int SMEM_BYTES = TILE_BYTES + 1024 + 256;
-// With the next-layer dot: one (HEAD_MAX_CLASSES + 1)-float slot per
-// epilogue thread, right after the 256 bytes of barriers.
-constexpr int SMEM_BYTES_DOT = SMEM_BYTES + 32 * 8 * (16 + 1) * 4;
+// With the next-layer dot: one slot of DOT_SLOT floats per epilogue thread,
+// right after the 256 bytes of barriers.  20 floats = 80 bytes keeps every
+// slot 16-byte aligned and the 128-bit accesses of 8 consecutive lanes on
+// distinct banks.
+constexpr int DOT_SLOT = 20;
+constexpr int SMEM_BYTES_DOT = SMEM_BYTES + 32 * 8 * DOT_SLOT * 4;
 constexpr int EPI_WARPS = 8;                         // 2 per TMEM lane quarter, 128 columns each
 constexpr int THREADS = 64 + 32 * EPI_WARPS;         // producer + MMA + epilogue warps
 constexpr int TMEM_COLS = 2 * BN;                    // two accumulator buffers
@@ -372,17 +375,44 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* ma
   }
 }
 
-// part[j] += a * W[n, j] for the next-layer dot (W read as hi + lo; every
-// lane of a warp reads the same column n, so the loads are broadcasts).  part
-// is the thread's own slot in shared memory: the epilogue's 128 accumulators
-// leave no registers for it.  volatile keeps each update a shared-memory
-// access instead of letting the compiler hold the sums in registers.
-__device__ __forceinline__ void dot_accum(const Epilogue& ep, int64_t n, float a,
-                                          volatile float* part) {
-  const float* wh = ep.dot_hi + n * ep.dot_ld;
-  const float* wl = ep.dot_lo + n * ep.dot_ld;
-  for (int j = 0; j < ep.dot_n; ++j)
-    part[j] = fmaf(a, __fadd_rn(__ldg(wh + j), __ldg(wl + j)), part[j]);
+__device__ __forceinline__ float4 lds128(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// part[j] += sum over the NC columns n_first + c of a[c] * W[n_first + c, j],
+// column by column in order (so each part[j] is one sequential FMA chain).
+// part lives in the thread's shared-memory slot (the epilogue's 128
+// accumulators leave no registers for it); it is held in registers only
+// for the group.  Every lane of a warp reads the same W row (a broadcast).
+// Classes are taken four at a time (one 128-bit slot access, one 128-bit W
+// load per column), and only as many quads as dot_n needs.
+template <int NC>
+__device__ __forceinline__ void dot_group(const Epilogue& ep, int64_t n_first, const float (&a)[NC],
+                                          uint32_t part) {
+  const float4* wr = reinterpret_cast<const float4*>(ep.dot_w + n_first * 16);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (4 * q >= ep.dot_n) break;
+    float4 s = lds128(part + 16 * q);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const float4 w = __ldg(wr + 4 * c + q);
+      s.x = fmaf(a[c], w.x, s.x);
+      s.y = fmaf(a[c], w.y, s.y);
+      s.z = fmaf(a[c], w.z, s.z);
+      s.w = fmaf(a[c], w.w, s.w);
+    }
+    sts128(part + 16 * q, s);
+  }
 }
 
 // Stores columns [n0, n0+32) of row m from acc[Q*32 .. Q*32+32) through the
@@ -391,8 +421,7 @@ __device__ __forceinline__ void dot_accum(const Epilogue& ep, int64_t n, float a
 // constant and the array stays in registers.
 template <int Q, bool kDot>
 __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, int64_t N, int64_t m,
-                                               int64_t n0, const float (&acc)[128],
-                                               volatile float* part) {
+                                               int64_t n0, const float (&acc)[128], uint32_t part) {
 #define v(i) acc[Q * 32 + (i)]
   if (m >= M) return;
   const bool full = (n0 + 32 <= N) && ((ep.ldc & 3) == 0);
@@ -403,7 +432,8 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
         store_epi(ep, m, n0 + j, v(j));
         if (kDot) {
           const float y = __fadd_rn(v(j), ep.bias[n0 + j]);
-          dot_accum(ep, n0 + j, y > 0.0f ? y : 0.0f, part);
+          const float a1[1] = {y > 0.0f ? y : 0.0f};
+          dot_group<1>(ep, n0 + j, a1, part);
         }
       }
     }
@@ -438,8 +468,8 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
       for (int e = 0; e < 4; ++e) {
         float y = __fadd_rn(x[e], ep.bias[n0 + 4 * q + e]);
         x[e] = y > 0.0f ? y : 0.0f;
-        if (kDot) dot_accum(ep, n0 + 4 * q + e, x[e], part);
       }
+      if (kDot) dot_group<4>(ep, n0 + 4 * q, x, part);
     } else if (ep.mode == EPI_MASK_SPLIT) {
       float4 a = mh[q], b = ml[q];
       x[0] = __fadd_rn(a.x, b.x) > 0.0f ? x[0] : 0.0f;
@@ -632,11 +662,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       if (!ok) break;
       const int64_t m = tm * BM + quarter * 32 + lane;
       const int64_t nb = tn * BN + half * 128;
-      // Dot slot of this epilogue thread: 17 floats apart (conflict-free).
-      volatile float* part = reinterpret_cast<volatile float*>(smem + TILE_BYTES + 256) +
-                             (threadIdx.x - 64) * (HEAD_MAX_CLASSES + 1);
-      if (kDot)
-        for (int j = 0; j < HEAD_MAX_CLASSES; ++j) part[j] = 0.0f;
+      // Dot slot of this epilogue thread (shared-memory address).
+      const uint32_t part = smem_u32(smem + TILE_BYTES + 256) + (threadIdx.x - 64) * DOT_SLOT * 4;
+      if (kDot) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sts128(part + 16 * q, make_float4(0.f, 0.f, 0.f, 0.f));
+      }
       if (nb < p.N) epilogue_chunk<0, kDot>(p.ep, p.M, p.N, m, nb, acc, part);
       if (nb + 32 < p.N) epilogue_chunk<1, kDot>(p.ep, p.M, p.N, m, nb + 32, acc, part);
       if (nb + 64 < p.N) epilogue_chunk<2, kDot>(p.ep, p.M, p.N, m, nb + 64, acc, part);
@@ -644,7 +675,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       if (kDot && m < p.M && nb < p.N) {
         // BN is a multiple of DOT_SLICE: nb / DOT_SLICE is this half-tile's slice.
         float* o = p.ep.dot_out + ((nb / DOT_SLICE) * p.M + m) * p.ep.dot_ldp;
-        for (int j = 0; j < p.ep.dot_n; ++j) o[j] = part[j];
+        float s[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v4 = lds128(part + 16 * q);
+          s[4 * q] = v4.x; s[4 * q + 1] = v4.y; s[4 * q + 2] = v4.z; s[4 * q + 3] = v4.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < p.ep.dot_n) o[j] = s[j];
       }
     }
   }
@@ -703,8 +742,8 @@ bool eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const Operand& 
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
   if (!operand_ok(A) || !operand_ok(B)) return false;
   if (ep.dot_out && (ep.mode != EPI_BIAS_RELU_SPLIT || ep.dot_n < 1 ||
-                     ep.dot_n > HEAD_MAX_CLASSES || ep.dot_ldp < ep.dot_n || !ep.dot_hi ||
-                     !ep.dot_lo || ep.dot_ld < ep.dot_n))
+                     ep.dot_n > HEAD_MAX_CLASSES || ep.dot_ldp < ep.dot_n || !ep.dot_w ||
+                     (reinterpret_cast<uintptr_t>(ep.dot_w) & 15) != 0))
     return false;
   return true;
 }
@@ -756,7 +795,7 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
   const int grid = (int)std::min<int64_t>(tiles, ctx->sm_count);
   static_assert(BN % DOT_SLICE == 0 && DOT_SLICE == 128, "one dot slice per epilogue half");
   static_assert(EPI_WARPS == 8 && HEAD_MAX_CLASSES == 16 && SMEM_BYTES_DOT <= 232448,
-                "dot slots: 256 epilogue threads x 17 floats");
+                "dot slots: 256 epilogue threads x DOT_SLOT floats");
   if (ep.dot_out) tc_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES_DOT, ctx->stream>>>(ma, mb, p);
   else tc_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
   count_launch(ctx);
@@ -872,6 +911,25 @@ orca_status head_logits(orca_ctx* ctx, const float* part, int64_t slices, int64_
   if (M <= 0) return ORCA_OK;
   head::logits_kernel<<<(unsigned)cdiv(M * C, 256), 256, 0, ctx->stream>>>(part, slices, M, C,
                                                                             ldp, bias, logits);
+  count_launch(ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
+
+__global__ void head_pack_kernel(const float* __restrict__ w_hi, const float* __restrict__ w_lo,
+                                 int64_t H, int C, float* __restrict__ packed) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= H * 16) return;
+  const int64_t n = i / 16;
+  const int j = (int)(i % 16);
+  packed[i] = j < C ? __fadd_rn(w_hi[n * C + j], w_lo[n * C + j]) : 0.0f;
+}
+
+orca_status head_pack_weights(orca_ctx* ctx, const float* w_hi, const float* w_lo, int64_t H,
+                              int C, float* packed) {
+  if (C < 1 || C > HEAD_MAX_CLASSES) return fail(ORCA_INVALID_ARGUMENT, "head_pack: C");
+  if (H <= 0) return ORCA_OK;
+  head_pack_kernel<<<(unsigned)cdiv(H * 16, 256), 256, 0, ctx->stream>>>(w_hi, w_lo, H, C, packed);
   count_launch(ctx);
   ORCA_CUDA_TRY(cudaGetLastError());
   return ORCA_OK;

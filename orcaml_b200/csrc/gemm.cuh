@@ -39,10 +39,9 @@ struct Epilogue {
   // activation a[m, n] also feeds the classifier layer's product.  Slice s of
   // 128 output columns writes, for j < dot_n (<= 16),
   //   dot_out[(s * M + m) * dot_ldp + j] = sum_{n in slice} a[m, n] * W[n, j]
-  // with W[n, j] = dot_hi[n * dot_ld + j] + dot_lo[...] (sequential FMA over n).
-  const float* dot_hi = nullptr;
-  const float* dot_lo = nullptr;
-  int64_t dot_ld = 0;
+  // (sequential FMA over n), W given as fp32 rows of 16 (zero past dot_n):
+  // W[n, j] = dot_w[n * 16 + j], 16-byte aligned (see head_pack_weights).
+  const float* dot_w = nullptr;
   int dot_n = 0;
   float* dot_out = nullptr;
   int64_t dot_ldp = 0;
@@ -79,6 +78,10 @@ orca_status head_logits(orca_ctx* ctx, const float* part, int64_t slices, int64_
 // over act: dZ[m, n] = act > 0 ? sum_j g[m, j] W[n, j] : 0 written as planes,
 // and dW[n, j] = sum_m act[m, n] g[m, j] (row blocks summed in order through
 // `part`, which needs head_part_floats(B, H, C) floats).
+// W_packed[n * 16 + j] = (w_hi + w_lo)[n * C + j] for j < C, 0 for C <= j < 16:
+// the classifier weights in the layout the next-layer dot reads.
+orca_status head_pack_weights(orca_ctx* ctx, const float* w_hi, const float* w_lo, int64_t H,
+                              int C, float* packed);
 int64_t head_row_blocks(int64_t B);
 int64_t head_part_floats(int64_t B, int64_t H, int C);
 orca_status head_backward(orca_ctx* ctx, int64_t B, int64_t H, int C, const float* g,

@@ -277,6 +277,7 @@ struct orca_mlp {
   bool use_head = false;
   float* host_stage = nullptr;       // pinned: [0] loss, [1] device error word
   float* head_part = nullptr;        // dot slices [S][B][head_ldp] or dW row-block partials
+  float* head_w = nullptr;           // classifier weights packed [H][16] for the dot
   int64_t head_ldp = 0;
   float* workspace = nullptr;
   size_t workspace_bytes = 0;
@@ -475,6 +476,7 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
     const int64_t fwd = cdiv(H, DOT_SLICE) * B * m->head_ldp;
     const int64_t bwd = head_part_floats(B, H, (int)C);
     ALLOC(head_part, (size_t)std::max(fwd, bwd) * 4);
+    ALLOC(head_w, (size_t)H * 16 * 4);
   }
 #undef ALLOC
   for (int l = 0; l < 64; ++l) m->ev_layer[l] = nullptr;
@@ -752,15 +754,14 @@ static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad) {
       // The classifier layer's product rides on this GEMM's epilogue when it
       // takes the tensor cores.
       Epilogue ed = ep;
-      ed.dot_hi = m->w_hi[L - 1];
-      ed.dot_lo = m->w_lo[L - 1];
-      ed.dot_ld = C;
+      ed.dot_w = m->head_w;
       ed.dot_n = (int)C;
       ed.dot_out = m->head_part;
       ed.dot_ldp = m->head_ldp;
       if (gemm_select(ctx, B, N, K, a, w, ed, m->gemm_path) == GEMM_TC) {
         ep = ed;
         fused_head = true;
+        ORCA_TRY(head_pack_weights(ctx, m->w_hi[L - 1], m->w_lo[L - 1], N, (int)C, m->head_w));
       }
     }
     const int path = gemm_select(ctx, B, N, K, a, w, ep, m->gemm_path);
