@@ -211,7 +211,8 @@ orca_status orca_linear_fwd(orca_ctx* ctx, const orca_buf* x, const orca_buf* w,
  * row-major, the reference's [in,out] layout, vs [n,k]), i.e. X@W, dY@W^T and
  * X^T@dY without materialised transposes (orca-autograd/src/backend.rs:
  * 1448-1499 transposes explicitly).  path: 0 auto, 1 SIMT FFMA, 2 tcgen05
- * (ORCA_INVALID_ARGUMENT when the shape/alignment does not allow it). */
+ * (ORCA_INVALID_ARGUMENT when the shape/alignment does not allow it), 3 / 4
+ * tcgen05 with the single-CTA / CTA-pair (256 x 256 tiles on two SMs) kernel. */
 orca_status orca_gemm_ex(orca_ctx* ctx, int64_t m, int64_t n, int64_t k, const orca_buf* a,
                          int a_mn_major, const orca_buf* b, int b_mn_major, int path,
                          orca_buf** out);
@@ -263,7 +264,8 @@ typedef struct {
   double lr, momentum, dampening, weight_decay;   /* SGD (sgd.py:30-44) */
   double beta1, beta2, eps;                       /* AdamW (adamw.py:24-38) */
   int gemm_path;             /* 0 auto (tcgen05 where shapes allow and the output has
-                                enough tiles), 1 SIMT FFMA only, 2 tcgen05 wherever allowed */
+                                enough tiles), 1 SIMT FFMA only, 2 tcgen05 wherever allowed;
+                                3 / 4 as 2 with the single-CTA / CTA-pair tcgen05 kernel */
 } orca_mlp_config;
 
 orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp** out);

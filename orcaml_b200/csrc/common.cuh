@@ -183,39 +183,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
-// Same wait for a barrier that the other CTA of a pair also arrives on
-// (acquire at cluster scope, so that CTA's prior writes are visible).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort, int* dev_err,
-                                                  unsigned sleep_ns = 0) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (sleep_ns) __nanosleep(sleep_ns);
-    if ((it & 63u) == 0) {
-      if (*abort) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        if (dev_err) atomicExch(dev_err, DEV_WAIT_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
-
 // ---------------------------------------------------------------- TMA
 // 3-D tiled bulk tensor load global -> shared, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
@@ -224,6 +191,18 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// The same load issued by the odd CTA of a pair, its completion counted on the
+// even CTA's barrier (bar_cl: shared::cluster address); the bytes land in
+// this CTA's own shared memory.
+__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const CUtensorMap* map,
+                                                 uint32_t bar_cl, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cl), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -293,9 +272,13 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
                "memory");
 }
+// Arrive on an mbarrier of either CTA of the pair (default semantics,
+// release at CTA scope: a cluster-scope release would put a full memory fence
+// on every hand-off, and the data these barriers guard -- shared memory
+// written by TMA, TMEM -- is ordered by the async-proxy completions and the
+// tcgen05 fences, not by this thread's own writes).
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cl_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
 }
 __device__ __forceinline__ void st_remote_u32(uint32_t cl_addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cl_addr), "r"(v) : "memory");

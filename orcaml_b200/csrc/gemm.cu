@@ -415,6 +415,18 @@ __device__ __forceinline__ void dot_group(const Epilogue& ep, int64_t n_first, c
   }
 }
 
+// load_operand for the odd CTA of a pair: completion on the even CTA's barrier.
+__device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMap* map,
+                                                  uint32_t bar_cl, int mn_major, int rows,
+                                                  int64_t mn0, int64_t k0) {
+  if (mn_major) {
+    for (int c = 0; c < rows / 32; ++c)
+      tma_load_3d_pair(dst + c * 4096, map, bar_cl, (int)(mn0 + 32 * c), (int)k0, 0);
+  } else {
+    tma_load_3d_pair(dst, map, bar_cl, (int)k0, (int)mn0, 0);
+  }
+}
+
 // Stores columns [n0, n0+32) of row m from acc[Q*32 .. Q*32+32) through the
 // epilogue (and, with kDot, adds their next-layer dot into part).  Q is a
 // template parameter so that every accumulator index is a compile-time
@@ -694,6 +706,278 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+// ---------------------------------------------------------------- CTA pairs
+// tc_gemm_pair_kernel: the same product on 256 x 256 output tiles, each
+// computed by a cluster of two CTAs on two SMs with tcgen05.mma.cta_group::2
+// (M = 256: rows [0,128) of the tile in the even CTA's TMEM, [128,256) in the
+// odd CTA's).  Each CTA stages its own 128 rows of A and 128 of the 256
+// columns of B, so per SM the shared-memory operand traffic per MMA is two
+// thirds of the single-CTA kernel's (A 4 KB + half of B 4 KB instead of
+// A 4 KB + B 8 KB per 8-deep k-step), with the same 192 KB of stages
+// (6 x 32 KB instead of 4 x 48 KB).
+//
+// Roles and hand-offs (E = even CTA, O = odd CTA):
+//   warp 0 (both): TMA loads of the CTA's own tiles into its own shared
+//     memory, all counted on E.full[stage] (E arms it for the bytes of both
+//     CTAs; O's loads use the cta_group::2 form that signals E's barrier);
+//     each waits on its own empty[stage].
+//   warp 1 (E): waits on E.full, issues the pair MMAs, commits to
+//     empty[stage] of both CTAs, and per accumulation chunk to tfull[buf] of
+//     both; waits on E.tempty[buf] (one arrival per epilogue warp of both
+//     CTAs) before reusing a TMEM buffer.
+//   warps 2-9 (both): epilogue of the CTA's own 128 rows, as in the single-CTA
+//     kernel.
+// A role that gives up (bounded wait) raises the abort flag of both CTAs.
+// O cannot observe its own copies' completion (they count on E's barrier),
+// so after an abort its producer waits 50 us past its last issue -- far
+// longer than a copy takes -- before the CTA may exit.  Both CTAs pass the
+// same two cluster barriers (after set-up, before TMEM release), with no
+// early exit between them.
+constexpr int PSTAGES = 6;
+constexpr int PB_ROWS = BN / 2;                      // B columns staged per CTA
+constexpr int PA_STAGE = A_STAGE;                    // 16 KB
+constexpr int PB_STAGE = 2 * PB_ROWS * BK * 4;       // 16 KB
+static_assert(PSTAGES * (PA_STAGE + PB_STAGE) == TILE_BYTES, "same stage budget as tc_gemm_kernel");
+static_assert(2 * PSTAGES + 5 <= 30, "barriers fit in the 256-byte barrier area");
+
+template <bool kDot>
+__global__ void __launch_bounds__(THREADS, 1)
+tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                    const __grid_constant__ CUtensorMap map_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* a_tiles = smem;
+  uint8_t* b_tiles = smem + PSTAGES * PA_STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TILE_BYTES);
+  uint64_t* full_bar = bars;                          // [PSTAGES] (E) both CTAs' bytes
+  uint64_t* empty_bar = bars + PSTAGES;               // [PSTAGES] stage consumed
+  uint64_t* tfull_bar = bars + 2 * PSTAGES;           // [2]
+  uint64_t* tempty_bar = bars + 2 * PSTAGES + 2;      // [2] (E) both epilogues drained
+  uint64_t* drain_bar = bars + 2 * PSTAGES + 4;       // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * PSTAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool even = rank == 0;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t num_m = cdiv(p.M, 2 * BM), num_n = cdiv(p.N, BN);
+  const int64_t num_tiles = num_m * num_n;
+  const int64_t cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int64_t nk = cdiv(p.K, BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 2 * EPI_WARPS);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t peer_abort = cluster_addr(const_cast<int*>(abort_flag), rank ^ 1u);
+  auto raise_abort = [&]() {
+    *abort_flag = 1;
+    st_remote_u32(peer_abort, 1u);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[PSTAGES];
+      for (int s = 0; s < PSTAGES; ++s) issued[s] = -1;
+      uint64_t last_issue = 0;
+      bool ok = true;
+      for (int64_t tile = cluster; tile < num_tiles && ok; tile += nclusters) {
+        int64_t tm, tn;
+        tile_coords(tile, num_m, num_n, tm, tn);
+        const int64_t a_row = tm * 2 * BM + (int64_t)rank * BM;
+        const int64_t b_col = tn * BN + (int64_t)rank * PB_ROWS;
+        for (int64_t kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.dev_err)) {
+            ok = false;
+            break;
+          }
+          if (even) {
+            mbar_arrive_expect_tx(&full_bar[stage], 2 * (PA_STAGE + PB_STAGE));
+            load_operand(a_tiles + stage * PA_STAGE, &map_a, &full_bar[stage], p.a_mn, BM, a_row,
+                         kb * BK);
+            load_operand(b_tiles + stage * PB_STAGE, &map_b, &full_bar[stage], p.b_mn, PB_ROWS,
+                         b_col, kb * BK);
+            issued[stage] = (int)phase;
+          } else {
+            const uint32_t bar_e = cluster_addr(&full_bar[stage], 0);
+            load_operand_pair(a_tiles + stage * PA_STAGE, &map_a, bar_e, p.a_mn, BM, a_row,
+                              kb * BK);
+            load_operand_pair(b_tiles + stage * PB_STAGE, &map_b, bar_e, p.b_mn, PB_ROWS, b_col,
+                              kb * BK);
+            last_issue = global_ns();
+          }
+          if (++stage == PSTAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        raise_abort();
+        if (!even && last_issue) {
+          while (global_ns() - last_issue < 50000ull) {
+          }
+        }
+      }
+      for (int s = 0; s < PSTAGES; ++s) {
+        if (issued[s] < 0) continue;
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(&full_bar[s], (uint32_t)issued[s]) &&
+               global_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (even && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer (even)
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)p.a_mn << 15) |
+                             ((uint32_t)p.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)((2 * BM) >> 4) << 24);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t chunk_ctr = 0;
+      bool ok = true;
+      const int F = p.chunk_kb;
+      const int nk32 = (int)nk;
+      for (int64_t tile = cluster; tile < num_tiles && ok; tile += nclusters) {
+        uint32_t d_tmem = tmem_base;
+        int buf = 0;
+        int in_chunk = 0;
+        for (int kb = 0; kb < nk32; ++kb) {
+          const bool chunk_start = in_chunk == 0;
+          if (chunk_start) {
+            buf = (int)(chunk_ctr & 1u);
+            const uint32_t use = chunk_ctr >> 1;
+            if (!mbar_wait(&tempty_bar[buf], (use & 1u) ^ 1u, abort_flag, p.dev_err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d_tmem = tmem_base + (uint32_t)(buf * BN);
+          }
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.dev_err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(a_tiles + stage * PA_STAGE);
+          const uint32_t b_base = smem_u32(b_tiles + stage * PB_STAGE);
+#pragma unroll
+          for (int ks = 0; ks < BK / 8; ++ks) {
+            const uint64_t a_hi = operand_desc(a_base, p.a_mn, BM, 0, ks);
+            const uint64_t a_lo = operand_desc(a_base, p.a_mn, BM, 1, ks);
+            const uint64_t b_hi = operand_desc(b_base, p.b_mn, PB_ROWS, 0, ks);
+            const uint64_t b_lo = operand_desc(b_base, p.b_mn, PB_ROWS, 1, ks);
+            const uint32_t first = (chunk_start && ks == 0) ? 0u : 1u;
+            tc_mma_tf32_pair(d_tmem, a_lo, b_hi, idesc, first);
+            tc_mma_tf32_pair(d_tmem, a_hi, b_lo, idesc, 1u);
+            tc_mma_tf32_pair(d_tmem, a_hi, b_hi, idesc, 1u);
+          }
+          tc_commit_pair(cluster_addr(&empty_bar[stage], 0));
+          tc_commit_pair(cluster_addr(&empty_bar[stage], 1));
+          if (++stage == PSTAGES) { stage = 0; phase ^= 1u; }
+          if (++in_chunk == F || kb == nk32 - 1) {
+            tc_commit_pair(cluster_addr(&tfull_bar[buf], 0));
+            tc_commit_pair(cluster_addr(&tfull_bar[buf], 1));
+            ++chunk_ctr;
+            in_chunk = 0;
+          }
+        }
+      }
+      if (!ok) raise_abort();
+      tc_commit_pair(cluster_addr(drain_bar, 0));
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain_bar, 0) && global_ns() - t0 < kWaitLimitNs) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) / 4;
+    const int nchunks = (int)cdiv(nk, p.chunk_kb);
+    const uint32_t tempty_even[2] = {cluster_addr(&tempty_bar[0], 0),
+                                     cluster_addr(&tempty_bar[1], 0)};
+    uint32_t chunk_ctr = 0;
+    bool ok = true;
+    for (int64_t tile = cluster; tile < num_tiles && ok; tile += nclusters) {
+      int64_t tm, tn;
+      tile_coords(tile, num_m, num_n, tm, tn);
+      float acc[128];
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+      for (int c = 0; c < nchunks; ++c) {
+        const int buf = (int)(chunk_ctr & 1u);
+        const uint32_t use = chunk_ctr >> 1;
+        if (!mbar_wait(&tfull_bar[buf], use & 1u, abort_flag, p.dev_err, 64)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                               (uint32_t)(buf * BN + half * 128);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float v[16];
+          tmem_ld_32x32b_x16(tbase + (uint32_t)(q * 16), v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[q * 16 + j] = __fadd_rn(acc[q * 16 + j], v[j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(tempty_even[buf]);
+        ++chunk_ctr;
+      }
+      if (!ok) break;
+      const int64_t m = tm * 2 * BM + (int64_t)rank * BM + quarter * 32 + lane;
+      const int64_t nb = tn * BN + half * 128;
+      const uint32_t part = smem_u32(smem + TILE_BYTES + 256) + (threadIdx.x - 64) * DOT_SLOT * 4;
+      if (kDot) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sts128(part + 16 * q, make_float4(0.f, 0.f, 0.f, 0.f));
+      }
+      if (nb < p.N) epilogue_chunk<0, kDot>(p.ep, p.M, p.N, m, nb, acc, part);
+      if (nb + 32 < p.N) epilogue_chunk<1, kDot>(p.ep, p.M, p.N, m, nb + 32, acc, part);
+      if (nb + 64 < p.N) epilogue_chunk<2, kDot>(p.ep, p.M, p.N, m, nb + 64, acc, part);
+      if (nb + 96 < p.N) epilogue_chunk<3, kDot>(p.ep, p.M, p.N, m, nb + 96, acc, part);
+      if (kDot && m < p.M && nb < p.N) {
+        float* o = p.ep.dot_out + ((nb / DOT_SLICE) * p.M + m) * p.ep.dot_ldp;
+        float sv[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v4 = lds128(part + 16 * q);
+          sv[4 * q] = v4.x; sv[4 * q + 1] = v4.y; sv[4 * q + 2] = v4.z; sv[4 * q + 3] = v4.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < p.ep.dot_n) o[j] = sv[j];
+      }
+    }
+    if (!ok) raise_abort();
+  }
+
+  __syncwarp();   // lanes that ran a role rejoin their warp before the aligned barrier
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+}
+
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -760,8 +1044,67 @@ static int64_t chunk_kblocks() {
   return v;
 }
 
+// The pair kernel is correct but measured ~4% slower than the single-CTA
+// kernel on the MLP's products (4096 x 8192 x 8192: 2.32 vs 2.23 ms on B200),
+// so AUTO/TC take it only when ORCA_GEMM_PAIR=1.
+static bool pair_enabled() {
+  static const bool v = [] {
+    const char* e = getenv("ORCA_GEMM_PAIR");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
+// Most clusters of two CTAs of a pair kernel that fit on the device at once.
+template <bool kDot>
+static orca_status pair_clusters(orca_ctx* ctx, int* out) {
+  static int cached[64] = {};
+  if (ctx->device < 64 && cached[ctx->device] > 0) {
+    *out = cached[ctx->device];
+    return ORCA_OK;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (ctx->sm_count / 2));
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = kDot ? SMEM_BYTES_DOT : SMEM_BYTES;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  ORCA_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, tc_gemm_pair_kernel<kDot>, &cfg));
+  if (n < 1) return fail(ORCA_CUDA_ERROR, "no cluster of two CTAs fits on the device");
+  if (ctx->device < 64) cached[ctx->device] = n;
+  *out = n;
+  return ORCA_OK;
+}
+
+template <bool kDot>
+static orca_status launch_pair(orca_ctx* ctx, const CUtensorMap& ma, const CUtensorMap& mb,
+                               const Params& p, int64_t tiles) {
+  int nclusters = 0;
+  ORCA_TRY(pair_clusters<kDot>(ctx, &nclusters));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(tiles, nclusters)));
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = kDot ? SMEM_BYTES_DOT : SMEM_BYTES;
+  cfg.stream = ctx->stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ORCA_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<kDot>, ma, mb, p));
+  return ORCA_OK;
+}
+
 orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
-                   const Operand& B, const Epilogue& ep) {
+                   const Operand& B, const Epilogue& ep, int path) {
   static bool attr_set[64] = {};
   if (ctx->device < 64 && !attr_set[ctx->device]) {
     ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<false>,
@@ -769,14 +1112,23 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
     ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<true>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES_DOT));
+    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_pair_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_pair_kernel<true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES_DOT));
     attr_set[ctx->device] = true;
   }
+  const bool pair = path == GEMM_TC_PAIR ||
+                    (path != GEMM_TC_SINGLE && pair_enabled() && M >= 2 * BM);
+  // B tile rows per CTA: all BN columns, or the CTA's half of them in a pair.
+  const int b_rows = pair ? PB_ROWS : BN;
   CUtensorMap ma, mb;
   // A: K-major rows = M (extent {K, M}); MN-major rows = K (extent {M, K}).
   if (A.mn_major) ORCA_TRY(make_map(&ma, A, M, K, 32, BK, true));
   else ORCA_TRY(make_map(&ma, A, K, M, BK, BM, false));
   if (B.mn_major) ORCA_TRY(make_map(&mb, B, N, K, 32, BK, true));
-  else ORCA_TRY(make_map(&mb, B, K, N, BK, BN, false));
+  else ORCA_TRY(make_map(&mb, B, K, N, BK, b_rows, false));
   Params p;
   p.M = M; p.N = N; p.K = K;
   p.a_mn = A.mn_major ? 1 : 0;
@@ -796,6 +1148,13 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
   static_assert(BN % DOT_SLICE == 0 && DOT_SLICE == 128, "one dot slice per epilogue half");
   static_assert(EPI_WARPS == 8 && HEAD_MAX_CLASSES == 16 && SMEM_BYTES_DOT <= 232448,
                 "dot slots: 256 epilogue threads x DOT_SLOT floats");
+  if (pair) {
+    const int64_t pair_tiles = cdiv(M, 2 * BM) * cdiv(N, BN);
+    if (ep.dot_out) ORCA_TRY(launch_pair<true>(ctx, ma, mb, p, pair_tiles));
+    else ORCA_TRY(launch_pair<false>(ctx, ma, mb, p, pair_tiles));
+    count_launch(ctx);
+    return ORCA_OK;
+  }
   if (ep.dot_out) tc_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES_DOT, ctx->stream>>>(ma, mb, p);
   else tc_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
   count_launch(ctx);
@@ -965,7 +1324,7 @@ orca_status head_backward(orca_ctx* ctx, int64_t B, int64_t H, int C, const floa
 static bool use_tc(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
                    const Operand& B, const Epilogue& ep, int path) {
   if (path == GEMM_SIMT || K <= 0 || !tc::eligible(M, N, K, A, B, ep)) return false;
-  if (path == GEMM_TC) return true;
+  if (gemm_path_is_tc(path)) return true;
   const int64_t tiles = cdiv(M, tc::BM) * cdiv(N, tc::BN);
   return tiles >= std::max<int64_t>(8, ctx->sm_count / 8);
 }
@@ -984,7 +1343,7 @@ orca_status gemm(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& 
                  const Operand& B, const Epilogue& ep, int path, float* workspace,
                  size_t workspace_bytes) {
   if (M <= 0 || N <= 0) return ORCA_OK;
-  if (use_tc(ctx, M, N, K, A, B, ep, path)) return tc::launch(ctx, M, N, K, A, B, ep);
+  if (use_tc(ctx, M, N, K, A, B, ep, path)) return tc::launch(ctx, M, N, K, A, B, ep, path);
   if (ep.dot_out)
     return fail(ORCA_INVALID_ARGUMENT, "gemm: the next-layer dot needs the tensor-core path");
 

@@ -53,7 +53,14 @@ constexpr int HEAD_MAX_CLASSES = 16;
 
 // AUTO: tensor cores when eligible and large enough; SIMT: FFMA kernels only;
 // TC: tensor cores whenever eligible (skinny/unaligned shapes still use SIMT).
-enum GemmPath : int { GEMM_AUTO = 0, GEMM_SIMT = 1, GEMM_TC = 2 };
+// On the tensor cores, AUTO and TC take the single-CTA kernel (the CTA-pair
+// kernel when the environment sets ORCA_GEMM_PAIR=1 and M >= 256);
+// TC_SINGLE and TC_PAIR force one or the other.
+enum GemmPath : int { GEMM_AUTO = 0, GEMM_SIMT = 1, GEMM_TC = 2, GEMM_TC_SINGLE = 3,
+                      GEMM_TC_PAIR = 4 };
+inline bool gemm_path_is_tc(int path) {
+  return path == GEMM_TC || path == GEMM_TC_SINGLE || path == GEMM_TC_PAIR;
+}
 
 // Enqueue on ctx->stream.  `workspace`/`workspace_bytes` may be null/0; the
 // split-K skinny kernels then allocate stream-ordered scratch.

@@ -374,6 +374,8 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
   ORCA_TRY(check_ctx(ctx));
   if (!cfg || !out || !cfg->dims) return fail(ORCA_INVALID_ARGUMENT, "null argument");
   if (cfg->n_layers < 1 || cfg->n_layers > 60) return fail(ORCA_INVALID_ARGUMENT, "n_layers");
+  if (cfg->gemm_path < GEMM_AUTO || cfg->gemm_path > GEMM_TC_PAIR)
+    return fail(ORCA_INVALID_ARGUMENT, "gemm_path must be in [0, 4]");
   if (cfg->batch < 1) return fail(ORCA_INVALID_ARGUMENT, "batch must be positive");
   for (int i = 0; i <= cfg->n_layers; ++i)
     if (cfg->dims[i] < 1) return fail(ORCA_INVALID_ARGUMENT, "dims must be positive");

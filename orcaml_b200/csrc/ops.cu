@@ -879,7 +879,7 @@ orca_status orca_gemm_ex(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const o
   ORCA_TRY(check_ctx(ctx));
   LOCK(ctx);
   if (!a || !b || !out) return fail(ORCA_INVALID_ARGUMENT, "null argument");
-  if (M < 0 || N < 0 || K < 0 || path < 0 || path > 2)
+  if (M < 0 || N < 0 || K < 0 || path < 0 || path > 4)
     return fail(ORCA_INVALID_ARGUMENT, "gemm_ex: bad arguments");
   ORCA_TRY(need(a, (size_t)(M * K), "gemm_ex"));
   ORCA_TRY(need(b, (size_t)(K * N), "gemm_ex"));
@@ -901,7 +901,7 @@ orca_status orca_gemm_ex(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const o
   ep.mode = EPI_STORE;
   ep.out = (float*)(*out)->ptr;
   ep.ldc = N;
-  if (path == GEMM_TC && !gemm_tc_eligible(M, N, K, oa, ob)) {
+  if (gemm_path_is_tc(path) && !gemm_tc_eligible(M, N, K, oa, ob)) {
     cudaFreeAsync(scratch, ctx->stream);
     orca_buf_release(*out);
     *out = nullptr;

@@ -22,7 +22,7 @@ from . import _lib as L
 from .backend import CudaBackend
 
 OPT = {"sgd": 0, "adamw": 1}
-GEMM_PATH = {"auto": 0, "simt": 1, "tc": 2}
+GEMM_PATH = {"auto": 0, "simt": 1, "tc": 2, "tc_single": 3, "tc_pair": 4}
 
 
 def _validate_float(name, value, positive=False):

@@ -54,6 +54,28 @@ def test_simt_and_skinny(be, m, n, k, a_mn, b_mn):
     assert_fp32_gemm(c, A, B)
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (False, False), (True, False)])
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (512, 768, 784), (300, 1000, 200),
+                                   (100, 256, 48), (1000, 300, 4096)])
+def test_tcgen05_cta_pair_kernel(be, m, n, k, a_mn, b_mn):
+    """The two-CTA kernel (256 x 256 tiles, cta_group::2): every orientation,
+    ragged M (an odd CTA whose rows all lie past M), ragged N and K."""
+    c, A, B = run(be, m, n, k, a_mn, b_mn, path=4)
+    assert_fp32_gemm(c, A, B)
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 512, 256), (384, 768, 784)])
+def test_tcgen05_single_cta_kernel_forced(be, m, n, k):
+    c, A, B = run(be, m, n, k, False, True, path=3)
+    assert_fp32_gemm(c, A, B)
+
+
+def test_tcgen05_pair_large_tiles_and_waves(be):
+    # More pair tiles than clusters: the persistent loop wraps on both CTAs.
+    c, A, B = run(be, 4096, 4096, 512, True, True, path=4)
+    assert_fp32_gemm(c, A, B)
+
+
 def test_tcgen05_is_not_plain_tf32(be):
     """A TF32-only product misses the FP32 bound by a wide margin; the
     split path meets it -- evidence that the lo planes are being used."""

@@ -103,11 +103,13 @@ def test_c0_free_running_tensor_core_path(be):
     tr.close()
 
 
-def test_first_step_gradients_match_oracle(be):
-    """All GEMM orientations (forward, dW, dX) and db on one step."""
+@pytest.mark.parametrize("path", ["tc", "tc_single", "tc_pair"])
+def test_first_step_gradients_match_oracle(be, path):
+    """All GEMM orientations (forward, dW, dX) and db on one step, on each
+    tensor-core kernel."""
     dims, B = [784, 512, 256, 10], 256
     x, t, _ = make_batch(dims, B, 3)
-    tr = make(be, dims, B, "sgd", "tc", lr=0.0)
+    tr = make(be, dims, B, "sgd", path, lr=0.0)
     tr.step(x, t)
     loss_ref, grads_ref, _ = O.mlp_forward_backward(dims, init_params(dims, 1), x, t)
     for i, (g, r) in enumerate(zip(tr.get_grads(), grads_ref)):
