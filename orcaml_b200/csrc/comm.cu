@@ -81,6 +81,9 @@ orca_status nccl_fail(ncclResult_t r, const char* what) {
 }
 
 // Poll a non-blocking communicator until its pending operation completes.
+// The first ~50 us spin (a collective's enqueue usually finishes within
+// microseconds, and a sleep here would stall the host's enqueue of the rest
+// of the step); after that the poll backs off to 50 us sleeps.
 orca_status wait_ready(orca_comm* c, const char* what) {
   NcclApi& a = api();
   auto t0 = std::chrono::steady_clock::now();
@@ -97,7 +100,8 @@ orca_status wait_ready(orca_comm* c, const char* what) {
       return fail(ORCA_TIMEOUT, "%s: no progress after %.1f s; communicator aborted", what,
                   c->timeout_s);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(100));
+    if (el < 50e-6) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
 }
 
