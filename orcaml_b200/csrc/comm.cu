@@ -15,6 +15,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 
@@ -155,6 +156,12 @@ orca_status orca_comm_init(orca_ctx* ctx, int rank, int world, const void* id, d
   memcpy(&uid, id, sizeof(uid));
   ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
   cfg.blocking = 0;
+  // ORCA_NCCL_MAX_CTAS caps the CTAs (SMs) a collective may occupy: the
+  // gradient all-reduce runs beside the next GEMM, which loses those SMs.
+  if (const char* e = getenv("ORCA_NCCL_MAX_CTAS")) {
+    const int v = atoi(e);
+    if (v > 0) cfg.maxCTAs = v;
+  }
   ncclResult_t r = a.CommInitRankConfig(&c->comm, world, uid, rank, &cfg);
   if (r != ncclSuccess && r != ncclInProgress) {
     ctx_release(ctx);

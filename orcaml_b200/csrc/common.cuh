@@ -57,6 +57,7 @@ struct orca_ctx {
   cudaStream_t stream = nullptr;        // compute stream
   cudaStream_t comm_stream = nullptr;   // collectives
   int* dev_err = nullptr;               // device error word (DeviceError)
+  int* tile_ctr = nullptr;              // tile counter of the persistent GEMM (reset per launch)
   double sync_timeout_s = 600.0;        // bound on every synchronising call
   cudaEvent_t sync_event = nullptr;
   std::mutex mu;

@@ -317,7 +317,14 @@ struct Params {
   int chunk_kb;            // k-blocks per accumulation chunk (>= 1)
   Epilogue ep;
   int* dev_err;
+  int* tile_ctr;           // zeroed before each launch of tc_gemm_kernel
+  int64_t tile_begin, tile_end;   // tiles [tile_begin, tile_end) of the raster order
 };
+
+// Dynamic tile scheduling of tc_gemm_kernel: the producer takes the next tile
+// index from a global counter and hands it to the MMA warp and the epilogue
+// warps through a ring of TQ shared-memory slots (-1 = no more tiles).
+constexpr int TQ = 4;
 
 // UMMA shared-memory matrix descriptor (sm_100 layout: start>>4 [0,14),
 // LBO>>4 [16,30), SBO>>4 [32,46), version 1 at [46,48), swizzle mode [61,64)).
@@ -515,12 +522,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   uint64_t* tfull_bar = bars + 2 * STAGES;   // [2]
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;  // [2]
   uint64_t* drain_bar = bars + 2 * STAGES + 4;   // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* tq_full = bars + 2 * STAGES + 5;     // [TQ] tile index published
+  uint64_t* tq_empty = tq_full + TQ;             // [TQ] read by the MMA and epilogue warps
+  volatile int* tile_q = reinterpret_cast<volatile int*>(tq_empty + TQ);   // [TQ]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tq_empty + TQ) + TQ;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int64_t num_m = cdiv(p.M, BM), num_n = cdiv(p.N, BN);
-  const int64_t num_tiles = num_m * num_n;
   const int64_t nk = cdiv(p.K, BK);
 
   if (threadIdx.x == 0) {
@@ -531,6 +540,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], 32 * EPI_WARPS);
+    }
+    for (int q = 0; q < TQ; ++q) {
+      mbar_init(&tq_full[q], 1);
+      mbar_init(&tq_empty[q], 1 + EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -557,9 +570,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       int issued[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = -1;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (uint32_t tq_i = 0; ok; ++tq_i) {
+        const int64_t t = p.tile_begin + atomicAdd(p.tile_ctr, 1);
+        const int slot = (int)(tq_i % TQ);
+        if (!mbar_wait(&tq_empty[slot], ((tq_i / TQ) & 1u) ^ 1u, abort_flag, p.dev_err)) {
+          ok = false;
+          break;
+        }
+        tile_q[slot] = t < p.tile_end ? (int)t : -1;
+        mbar_arrive(&tq_full[slot]);
+        if (t >= p.tile_end) break;
         int64_t tm, tn;
-        tile_coords(tile, num_m, num_n, tm, tn);
+        tile_coords(t, num_m, num_n, tm, tn);
         for (int64_t kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.dev_err, 20)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[stage], A_STAGE + B_STAGE);
@@ -592,7 +614,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       bool ok = true;
       const int F = p.chunk_kb;
       const int nk32 = (int)nk;
-      for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (uint32_t tq_i = 0; ok; ++tq_i) {
+        const int slot = (int)(tq_i % TQ);
+        if (!mbar_wait(&tq_full[slot], (tq_i / TQ) & 1u, abort_flag, p.dev_err)) {
+          ok = false;
+          break;
+        }
+        const int tile = tile_q[slot];
+        mbar_arrive(&tq_empty[slot]);
+        if (tile < 0) break;
         uint32_t d_tmem = tmem_base;
         int buf = 0;
         int in_chunk = 0;                 // k-blocks issued into the current chunk
@@ -647,7 +677,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int nchunks = (int)cdiv(nk, p.chunk_kb);
     uint32_t chunk_ctr = 0;
     bool ok = true;
-    for (int64_t tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (uint32_t tq_i = 0; ok; ++tq_i) {
+      const int slot = (int)(tq_i % TQ);
+      if (!mbar_wait(&tq_full[slot], (tq_i / TQ) & 1u, abort_flag, p.dev_err, 64)) {
+        ok = false;
+        break;
+      }
+      const int tile = tile_q[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tq_empty[slot]);
+      if (tile < 0) break;
       int64_t tm, tn;
       tile_coords(tile, num_m, num_n, tm, tn);
       float acc[128];   // 0 + x == x: the first chunk adds into zeros exactly
@@ -1104,7 +1143,7 @@ static orca_status launch_pair(orca_ctx* ctx, const CUtensorMap& ma, const CUten
 }
 
 orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
-                   const Operand& B, const Epilogue& ep, int path) {
+                   const Operand& B, const Epilogue& ep, int path, const TileRange* range) {
   static bool attr_set[64] = {};
   if (ctx->device < 64 && !attr_set[ctx->device]) {
     ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<false>,
@@ -1119,8 +1158,8 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
                                        SMEM_BYTES_DOT));
     attr_set[ctx->device] = true;
   }
-  const bool pair = path == GEMM_TC_PAIR ||
-                    (path != GEMM_TC_SINGLE && pair_enabled() && M >= 2 * BM);
+  const bool pair = !range && (path == GEMM_TC_PAIR ||
+                               (path != GEMM_TC_SINGLE && pair_enabled() && M >= 2 * BM));
   // B tile rows per CTA: all BN columns, or the CTA's half of them in a pair.
   const int b_rows = pair ? PB_ROWS : BN;
   CUtensorMap ma, mb;
@@ -1135,6 +1174,7 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
   p.b_mn = B.mn_major ? 1 : 0;
   p.ep = ep;
   p.dev_err = ctx->dev_err;
+  p.tile_ctr = ctx->tile_ctr;
   // Measured on B200 (mean |error| / sum|a*b|, relu-activation x weight data):
   // 8 k-blocks per chunk gives 1.6e-8 at K = 8192 and 5e-8 at K = 784, 4 gives
   // 2.6e-8 at K = 784; a single chain gives 1.0e-6 at K = 8192.  Serial FP32
@@ -1144,7 +1184,16 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
                        : (nk <= 64 ? SHORT_K_CHUNK_KB : DEFAULT_CHUNK_KB);
   p.chunk_kb = (int)std::max<int64_t>(1, std::min<int64_t>(nk, want));
   const int64_t tiles = cdiv(M, BM) * cdiv(N, BN);
-  const int grid = (int)std::min<int64_t>(tiles, ctx->sm_count);
+  p.tile_begin = 0;
+  p.tile_end = tiles;
+  int max_ctas = ctx->sm_count;
+  if (range) {
+    p.tile_begin = std::max<int64_t>(0, std::min<int64_t>(range->begin, tiles));
+    p.tile_end = range->end < 0 ? tiles : std::max(p.tile_begin, std::min(range->end, tiles));
+    if (range->max_ctas > 0) max_ctas = std::min(max_ctas, range->max_ctas);
+  }
+  if (p.tile_end <= p.tile_begin) return ORCA_OK;
+  const int grid = (int)std::min<int64_t>(p.tile_end - p.tile_begin, max_ctas);
   static_assert(BN % DOT_SLICE == 0 && DOT_SLICE == 128, "one dot slice per epilogue half");
   static_assert(EPI_WARPS == 8 && HEAD_MAX_CLASSES == 16 && SMEM_BYTES_DOT <= 232448,
                 "dot slots: 256 epilogue threads x DOT_SLOT floats");
@@ -1155,6 +1204,7 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
     count_launch(ctx);
     return ORCA_OK;
   }
+  ORCA_CUDA_TRY(cudaMemsetAsync(ctx->tile_ctr, 0, sizeof(int), ctx->stream));
   if (ep.dot_out) tc_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES_DOT, ctx->stream>>>(ma, mb, p);
   else tc_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
   count_launch(ctx);
@@ -1339,11 +1389,16 @@ bool gemm_tc_eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const O
   return tc::eligible(M, N, K, A, B, ep);
 }
 
+int64_t gemm_tc_tiles(int64_t M, int64_t N) { return cdiv(M, tc::BM) * cdiv(N, tc::BN); }
+
 orca_status gemm(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
                  const Operand& B, const Epilogue& ep, int path, float* workspace,
-                 size_t workspace_bytes) {
+                 size_t workspace_bytes, const TileRange* range) {
   if (M <= 0 || N <= 0) return ORCA_OK;
-  if (use_tc(ctx, M, N, K, A, B, ep, path)) return tc::launch(ctx, M, N, K, A, B, ep, path);
+  if (use_tc(ctx, M, N, K, A, B, ep, path))
+    return tc::launch(ctx, M, N, K, A, B, ep, path, range);
+  if (range && (range->begin > 0 || range->end >= 0))
+    return fail(ORCA_INVALID_ARGUMENT, "gemm: a tile range needs the tensor-core path");
   if (ep.dot_out)
     return fail(ORCA_INVALID_ARGUMENT, "gemm: the next-layer dot needs the tensor-core path");
 

@@ -64,9 +64,21 @@ inline bool gemm_path_is_tc(int path) {
 
 // Enqueue on ctx->stream.  `workspace`/`workspace_bytes` may be null/0; the
 // split-K skinny kernels then allocate stream-ordered scratch.
+// Part of the single-CTA tensor-core product: the tiles [begin, end) of its
+// raster order, on at most max_ctas CTAs (0 = one per SM).  Two launches over
+// [0, t) on fewer CTAs and [t, tiles) on all of them leave SMs free for a
+// collective during the first (see mlp.cu).
+struct TileRange {
+  int64_t begin = 0, end = -1;   // end < 0: to the last tile
+  int max_ctas = 0;
+};
+
 orca_status gemm(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand& A,
                  const Operand& B, const Epilogue& ep, int path,
-                 float* workspace = nullptr, size_t workspace_bytes = 0);
+                 float* workspace = nullptr, size_t workspace_bytes = 0,
+                 const TileRange* range = nullptr);
+// Number of tiles of the single-CTA tensor-core kernel for an M x N output.
+int64_t gemm_tc_tiles(int64_t M, int64_t N);
 
 // Whether the tcgen05 kernel can take these operands at all.
 bool gemm_tc_eligible(int64_t M, int64_t N, int64_t K, const Operand& A, const Operand& B);

@@ -285,14 +285,14 @@ struct orca_mlp {
   // data parallel
   orca_comm* comm = nullptr;
   size_t bucket_bytes = 0;
-  cudaEvent_t ev_layer[64];
-  cudaEvent_t ev_comm_done = nullptr;
+  cudaEvent_t ev_layer[64];         // layer's gradients ready (compute stream)
+  cudaEvent_t ev_reduced[64];       // layer's gradients averaged (comm stream)
   int last_launches = 0;
   // Optional per-kernel-group timing: CUDA events recorded on the compute
   // stream around each group of a step while profiling is on.
   struct ProfSite { std::string name; double flops = 0, bytes = 0; double ms = 0; int count = 0;
                     int gemm_path = -1; };
-  struct ProfRec { int site; cudaEvent_t a, b; };
+  struct ProfRec { int site; cudaEvent_t a, b; cudaStream_t stream; };
   bool profiling = false;
   std::vector<ProfSite> sites;
   std::vector<ProfRec> recs;
@@ -312,7 +312,7 @@ static cudaEvent_t pool_event(orca_mlp* m) {
 
 // Opens a timed group; returns a record index (or -1 when not profiling).
 static int prof_open(orca_mlp* m, const std::string& name, double flops, double bytes,
-                     int gemm_path = -1) {
+                     int gemm_path = -1, cudaStream_t stream = nullptr) {
   if (!m->profiling) return -1;
   int site = -1;
   for (size_t i = 0; i < m->sites.size(); ++i)
@@ -330,14 +330,15 @@ static int prof_open(orca_mlp* m, const std::string& name, double flops, double 
   r.site = site;
   r.a = pool_event(m);
   r.b = pool_event(m);
-  cudaEventRecord(r.a, m->ctx->stream);
+  r.stream = stream ? stream : m->ctx->stream;
+  cudaEventRecord(r.a, r.stream);
   m->recs.push_back(r);
   return (int)m->recs.size() - 1;
 }
 
 static void prof_close(orca_mlp* m, int rec) {
   if (rec < 0) return;
-  cudaEventRecord(m->recs[rec].b, m->ctx->stream);
+  cudaEventRecord(m->recs[rec].b, m->recs[rec].stream);
 }
 
 static orca_status mlp_alloc(orca_mlp* m, void** p, size_t bytes) {
@@ -481,12 +482,11 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
     ALLOC(head_w, (size_t)H * 16 * 4);
   }
 #undef ALLOC
-  for (int l = 0; l < 64; ++l) m->ev_layer[l] = nullptr;
+  for (int l = 0; l < 64; ++l) m->ev_layer[l] = m->ev_reduced[l] = nullptr;
   for (int l = 0; l < L; ++l)
-    if (cudaEventCreateWithFlags(&m->ev_layer[l], cudaEventDisableTiming) != cudaSuccess)
+    if (cudaEventCreateWithFlags(&m->ev_layer[l], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&m->ev_reduced[l], cudaEventDisableTiming) != cudaSuccess)
       return cleanup(fail(ORCA_CUDA_ERROR, "event creation failed"));
-  if (cudaEventCreateWithFlags(&m->ev_comm_done, cudaEventDisableTiming) != cudaSuccess)
-    return cleanup(fail(ORCA_CUDA_ERROR, "event creation failed"));
   if (sync_stream(ctx) != ORCA_OK) return cleanup(ORCA_CUDA_ERROR);
   *out = m;
   return ORCA_OK;
@@ -501,7 +501,8 @@ orca_status orca_mlp_destroy(orca_mlp* m) {
   if (m->host_stage) cudaFreeHost(m->host_stage);
   for (int l = 0; l < 64; ++l)
     if (m->ev_layer[l]) cudaEventDestroy(m->ev_layer[l]);
-  if (m->ev_comm_done) cudaEventDestroy(m->ev_comm_done);
+  for (int l = 0; l < 64; ++l)
+    if (m->ev_reduced[l]) cudaEventDestroy(m->ev_reduced[l]);
   for (auto& r : m->recs) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
   for (auto e : m->event_pool) cudaEventDestroy(e);
   orca_ctx* ctx = m->ctx;
@@ -793,6 +794,29 @@ static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad) {
   return ORCA_OK;
 }
 
+// SMs left to a gradient all-reduce during the dX GEMM that follows it, and
+// the share of that GEMM's tiles run on the remaining SMs (ORCA_COMM_SMS,
+// ORCA_COMM_SPLIT).  Off by default: measured at 2 GPUs, giving
+// the all-reduce 16 or 24 SMs made the GEMM 0.3-0.55 ms slower while the
+// all-reduce, contending for memory with it, still took 1.4-2.1 ms; the step
+// was 1.5-3 % slower than with the GEMM on every SM.
+struct CommOverlap {
+  int reserve_sms;
+  double first_fraction;
+};
+static CommOverlap comm_overlap() {
+  static const CommOverlap v = [] {
+    CommOverlap o{0, 0.5};
+    if (const char* e = getenv("ORCA_COMM_SMS")) o.reserve_sms = std::max(0, atoi(e));
+    if (const char* e = getenv("ORCA_COMM_SPLIT")) {
+      const double f = atof(e);
+      if (f > 0.0 && f < 1.0) o.first_fraction = f;
+    }
+    return o;
+  }();
+  return v;
+}
+
 static orca_status launch_layer_allreduce(orca_mlp* m, int l) {
   orca_ctx* ctx = m->ctx;
   ORCA_CUDA_TRY(cudaEventRecord(m->ev_layer[l], ctx->stream));
@@ -800,11 +824,17 @@ static orca_status launch_layer_allreduce(orca_mlp* m, int l) {
   // The layer's (dW, db) are contiguous in the arena.
   float* base = m->grads + m->p_off[2 * l];
   size_t n = (size_t)(m->dims[l] * m->dims[l + 1] + m->dims[l + 1]);
+  // Timed on the comm stream: from the layer's gradients being ready to
+  // their average being complete (includes waiting for SMs).
+  const int pr = prof_open(m, "allreduce_l" + std::to_string(l), 0.0, 4.0 * (double)n, -1,
+                           ctx->comm_stream);
   size_t chunk = m->bucket_bytes ? std::max<size_t>(m->bucket_bytes / 4, 1) : n;
   for (size_t off = 0; off < n; off += chunk) {
     size_t c = std::min(chunk, n - off);
     ORCA_TRY(comm_allreduce_avg_stream(m->comm, base + off, c, ctx->comm_stream));
   }
+  prof_close(m, pr);
+  ORCA_CUDA_TRY(cudaEventRecord(m->ev_reduced[l], ctx->comm_stream));
   return ORCA_OK;
 }
 
@@ -877,20 +907,35 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
     ex.ldc = K;
     ex.mask_hi = m->act_planes[l];
     ex.mask_lo = m->act_planes[l] + B * K;
+    const int dx_path = gemm_select(ctx, B, K, N, ga, wt, ex, m->gemm_path);
     pr = prof_open(m, "gemm_dx_l" + std::to_string(l), 2.0 * B * N * K,
-                   4.0 * ((g_lo ? 2 : 1) * B * N + 2 * K * N + 4 * B * K),
-                   gemm_select(ctx, B, K, N, ga, wt, ex, m->gemm_path));
-    ORCA_TRY(gemm(ctx, B, K, N, ga, wt, ex, m->gemm_path, m->workspace, m->workspace_bytes));
+                   4.0 * ((g_lo ? 2 : 1) * B * N + 2 * K * N + 4 * B * K), dx_path);
+    const CommOverlap ov = comm_overlap();
+    if (m->comm && dx_path == GEMM_TC && ov.reserve_sms > 0 && ov.reserve_sms < ctx->sm_count) {
+      // This layer's gradient all-reduce was just queued on the comm stream.
+      // The persistent GEMM would take every SM before the collective's CTAs
+      // are dispatched, so its first part runs on fewer CTAs and leaves
+      // reserve_sms SMs to the all-reduce; the rest runs on all SMs.
+      const int64_t tiles = gemm_tc_tiles(B, K);
+      TileRange first, rest;
+      first.end = (int64_t)(ov.first_fraction * (double)tiles);
+      first.max_ctas = ctx->sm_count - ov.reserve_sms;
+      rest.begin = first.end;
+      ORCA_TRY(gemm(ctx, B, K, N, ga, wt, ex, m->gemm_path, m->workspace, m->workspace_bytes,
+                    &first));
+      ORCA_TRY(gemm(ctx, B, K, N, ga, wt, ex, m->gemm_path, m->workspace, m->workspace_bytes,
+                    &rest));
+    } else {
+      ORCA_TRY(gemm(ctx, B, K, N, ga, wt, ex, m->gemm_path, m->workspace, m->workspace_bytes));
+    }
     prof_close(m, pr);
     g_hi = ex.out;
     g_lo = ex.out_lo;
     g_ld = K;
     cur ^= 1;
   }
-  if (m->comm) {
-    ORCA_CUDA_TRY(cudaEventRecord(m->ev_comm_done, ctx->comm_stream));
-    ORCA_CUDA_TRY(cudaStreamWaitEvent(ctx->stream, m->ev_comm_done, 0));
-  }
+  // With a communicator the optimizer waits per layer (mlp_update_impl), so
+  // the update of the layers reduced first overlaps the last all-reduce.
   return ORCA_OK;
 }
 
@@ -902,8 +947,12 @@ static orca_status mlp_update_impl(orca_mlp* m) {
   // momentum adds v read + write (20 B); AdamW reads p, g, m, v, writes p, m, v (28 B).
   const double bpp = m->opt == ORCA_OPT_ADAMW ? 28.0 : (m->mom != 0.0 ? 20.0 : 12.0);
   const int pr = prof_open(m, "optimizer", 0.0, bpp * (double)m->n_params);
-  for (int l = 0; l < L; ++l) {
+  // Last layer first: that is the order the backward pass (and the gradient
+  // all-reduce) finishes the layers in.  Each parameter's update is
+  // independent, so the order does not change any result.
+  for (int l = L - 1; l >= 0; --l) {
     const int64_t K = m->dims[l], N = m->dims[l + 1];
+    if (m->comm) ORCA_CUDA_TRY(cudaStreamWaitEvent(ctx->stream, m->ev_reduced[l], 0));
     for (int which = 0; which < 2; ++which) {
       const int idx = 2 * l + which;
       const int64_t n = which == 0 ? K * N : N;

@@ -65,6 +65,7 @@ void ctx_release(orca_ctx* ctx) {
   sync_stream_for(ctx, ctx->stream, ctx->sync_timeout_s);
   sync_stream_for(ctx, ctx->comm_stream, ctx->sync_timeout_s);
   cudaFree(ctx->dev_err);
+  cudaFree(ctx->tile_ctr);
   if (ctx->sync_event) cudaEventDestroy(ctx->sync_event);
   cudaStreamDestroy(ctx->stream);
   cudaStreamDestroy(ctx->comm_stream);
@@ -398,10 +399,17 @@ orca_status orca_ctx_create(int device, orca_ctx** out) {
   c->device = device;
   c->sm_count = prop.multiProcessorCount;
   ORCA_CUDA_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
-  ORCA_CUDA_TRY(cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking));
+  // Collectives get the highest stream priority: when a GEMM CTA retires, a
+  // waiting all-reduce takes the SM before more GEMM CTAs do (the GEMM's
+  // dynamic tile scheduler lets the CTAs that start later take fewer tiles).
+  int prio_low = 0, prio_high = 0;
+  ORCA_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high));
+  ORCA_CUDA_TRY(cudaStreamCreateWithPriority(&c->comm_stream, cudaStreamNonBlocking, prio_high));
   ORCA_CUDA_TRY(cudaEventCreateWithFlags(&c->sync_event, cudaEventDisableTiming));
   ORCA_CUDA_TRY(cudaMalloc(&c->dev_err, sizeof(int)));
   ORCA_CUDA_TRY(cudaMemset(c->dev_err, 0, sizeof(int)));
+  ORCA_CUDA_TRY(cudaMalloc(&c->tile_ctr, sizeof(int)));
+  ORCA_CUDA_TRY(cudaMemset(c->tile_ctr, 0, sizeof(int)));
   // Keep freed stream-ordered allocations in the pool instead of returning
   // them to the driver at every synchronisation.
   cudaMemPool_t pool;

@@ -27,11 +27,12 @@ from orcaml_b200.backend import CudaBackend
 from orcaml_b200.mlp import MlpTrainer
 from orcaml_b200.distributed import DistributedDataParallel
 from orcaml_b200.synthetic import init_params, make_batch
-rank, world, port, dims, batch, steps, opt = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]), \
-    json.loads(sys.argv[4]), int(sys.argv[5]), int(sys.argv[6]), sys.argv[7]
+rank, world, port, dims, batch, steps, opt, path = int(sys.argv[1]), int(sys.argv[2]), \
+    int(sys.argv[3]), json.loads(sys.argv[4]), int(sys.argv[5]), int(sys.argv[6]), sys.argv[7], \
+    sys.argv[8]
 be = CudaBackend(rank)
 kw = dict(lr=1e-3, weight_decay=0.01) if opt == "adamw" else dict(lr=0.01, momentum=0.9)
-tr = MlpTrainer(be, dims, batch, optimizer=opt, **kw)
+tr = MlpTrainer(be, dims, batch, optimizer=opt, gemm_path=path, **kw)
 tr.set_parameters(init_params(dims, 1))
 ddp = DistributedDataParallel(tr, rank=rank, world_size=world, master_addr=f"127.0.0.1:{port}",
                               timeout=60.0, bucket_bytes=1 << 20)
@@ -53,15 +54,19 @@ def _gpus():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("opt,dims,batch", [("adamw", [784, 256, 256, 10], 64),
-                                            ("sgd", [784, 1024, 1024, 10], 512)])
-def test_ddp_two_gpus_matches_oracle(tmp_path, opt, dims, batch):
+@pytest.mark.parametrize("opt,dims,batch,path", [("adamw", [784, 256, 256, 10], 64, "auto"),
+                                                 ("sgd", [784, 1024, 1024, 10], 512, "tc")])
+def test_ddp_two_gpus_matches_oracle(tmp_path, opt, dims, batch, path):
+    """The "tc" case runs the hidden layers on the tensor cores, so the dX GEMM
+    after each gradient all-reduce is split into two launches (the first on
+    fewer CTAs, leaving SMs to the collective)."""
     from oracle import oracle as O
     from orcaml_b200.synthetic import init_params, make_batch
     steps, world, port = 10, 2, 29411 + batch
     code = f"REPO = {REPO!r}\nOUT = {str(tmp_path)!r}\n" + WORKER
+    env = dict(os.environ, ORCA_COMM_SMS="16")   # exercise the split dX GEMM
     procs = [subprocess.Popen([sys.executable, "-c", code, str(r), str(world), str(port),
-                               json.dumps(dims), str(batch), str(steps), opt])
+                               json.dumps(dims), str(batch), str(steps), opt, path], env=env)
              for r in range(world)]
     try:
         for p in procs:
