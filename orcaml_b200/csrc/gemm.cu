@@ -1221,7 +1221,7 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
 // share one pass over the activation.
 namespace head {
 constexpr int THREADS = 256;
-constexpr int ROW_CHUNK = 256;        // rows of g staged in shared memory at a time
+constexpr int ROW_CHUNK = 128;        // rows of g staged in shared memory at a time
 constexpr int MAX_ROW_BLOCKS = 64;
 
 __global__ void __launch_bounds__(256)
@@ -1236,80 +1236,128 @@ logits_kernel(const float* __restrict__ part, int64_t slices, int64_t M, int C, 
   logits[i] = __fadd_rn(s, bias[j]);
 }
 
-// Thread per activation column n; a block covers 256 columns and one block of
-// rows, walking it in order.  Per row: one masked dot over the C classes
-// (dX, same FMA order as the plain product) and C FMAs into the column's dW
-// partial.
+// Thread per COLS adjacent activation columns; a block covers THREADS * COLS
+// columns and one block of rows, walking it in order.  Per row: one masked
+// dot over the C classes (dX, same FMA order as the plain product), C FMAs
+// into each column's dW partial, and the masked value into the column's sum
+// (the bias gradient of the layer below).  The dlogits rows are staged in
+// shared memory, CP (C rounded up to 4) floats per row, read as 128-bit
+// broadcasts.
+template <int CP, int COLS>
 __global__ void __launch_bounds__(THREADS)
 bwd_kernel(int64_t B, int64_t H, int C, int64_t rows, const float* __restrict__ g,
            const float* __restrict__ a_hi, const float* __restrict__ a_lo,
            const float* __restrict__ w_hi, const float* __restrict__ w_lo,
-           float* __restrict__ dz_hi, float* __restrict__ dz_lo, float* __restrict__ part) {
-  __shared__ float gs[ROW_CHUNK * HEAD_MAX_CLASSES];
-  const int64_t n = (int64_t)blockIdx.x * THREADS + threadIdx.x;
+           float* __restrict__ dz_hi, float* __restrict__ dz_lo, float* __restrict__ part,
+           float* __restrict__ db_part) {
+  __shared__ __align__(16) float gs[ROW_CHUNK * CP];
+  const int64_t n0 = ((int64_t)blockIdx.x * THREADS + threadIdx.x) * COLS;
   const int64_t m_begin = (int64_t)blockIdx.y * rows;
   const int64_t m_end = std::min<int64_t>(B, m_begin + rows);
-  const bool active = n < H;
-  float w[HEAD_MAX_CLASSES], dw[HEAD_MAX_CLASSES];
+  const bool active = n0 < H;   // H % COLS == 0
+  float w[COLS][CP], dw[COLS][CP], db[COLS];
 #pragma unroll
-  for (int j = 0; j < HEAD_MAX_CLASSES; ++j) {
-    w[j] = (active && j < C) ? __fadd_rn(w_hi[n * C + j], w_lo[n * C + j]) : 0.0f;
-    dw[j] = 0.0f;
+  for (int c = 0; c < COLS; ++c) {
+    db[c] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < CP; ++j) {
+      const int64_t wi = (n0 + c) * C + j;
+      w[c][j] = (active && j < C) ? __fadd_rn(w_hi[wi], w_lo[wi]) : 0.0f;
+      dw[c][j] = 0.0f;
+    }
   }
   for (int64_t c0 = m_begin; c0 < m_end; c0 += ROW_CHUNK) {
     const int nr = (int)std::min<int64_t>(ROW_CHUNK, m_end - c0);
     __syncthreads();
-    for (int e = threadIdx.x; e < nr * HEAD_MAX_CLASSES; e += THREADS) {
-      const int r = e / HEAD_MAX_CLASSES, j = e % HEAD_MAX_CLASSES;
+    for (int e = threadIdx.x; e < nr * CP; e += THREADS) {
+      const int r = e / CP, j = e % CP;
       gs[e] = j < C ? g[(c0 + r) * C + j] : 0.0f;
     }
     __syncthreads();
     if (!active) continue;
-    int r = 0;
-    for (; r < nr; r += 4) {
+    for (int r = 0; r < nr; r += 4) {
       const int cnt = std::min(4, nr - r);
-      float a[4];
+      float a[4][COLS];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int64_t idx = (c0 + r + u) * H + n;
-        a[u] = u < cnt ? __fadd_rn(a_hi[idx], a_lo[idx]) : 0.0f;
+        const int64_t idx = (c0 + r + u) * H + n0;
+        if (u < cnt) {
+          if (COLS == 2) {
+            const float2 h = *reinterpret_cast<const float2*>(a_hi + idx);
+            const float2 l = *reinterpret_cast<const float2*>(a_lo + idx);
+            a[u][0] = __fadd_rn(h.x, l.x);
+            a[u][COLS - 1] = __fadd_rn(h.y, l.y);
+          } else {
+            a[u][0] = __fadd_rn(a_hi[idx], a_lo[idx]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < COLS; ++c) a[u][c] = 0.0f;
+        }
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (u >= cnt) break;
-        const float* gr = gs + (r + u) * HEAD_MAX_CLASSES;
-        float d = 0.0f;
+        float gr[CP];
 #pragma unroll
-        for (int j = 0; j < HEAD_MAX_CLASSES; ++j)
-          if (j < C) d = fmaf(gr[j], w[j], d);
-        const float gv = a[u] > 0.0f ? d : 0.0f;
-        float h, l;
-        split_tf32(gv, h, l);
-        const int64_t idx = (c0 + r + u) * H + n;
-        dz_hi[idx] = h;
-        dz_lo[idx] = l;
+        for (int q = 0; q < CP / 4; ++q) {
+          const float4 v = *reinterpret_cast<const float4*>(gs + (r + u) * CP + 4 * q);
+          gr[4 * q] = v.x; gr[4 * q + 1] = v.y; gr[4 * q + 2] = v.z; gr[4 * q + 3] = v.w;
+        }
+        float hv[COLS], lv[COLS];
 #pragma unroll
-        for (int j = 0; j < HEAD_MAX_CLASSES; ++j)
-          if (j < C) dw[j] = fmaf(a[u], gr[j], dw[j]);
+        for (int c = 0; c < COLS; ++c) {
+          float d = 0.0f;
+#pragma unroll
+          for (int j = 0; j < CP; ++j)
+            if (j < C) d = fmaf(gr[j], w[c][j], d);
+          const float gv = a[u][c] > 0.0f ? d : 0.0f;
+          split_tf32(gv, hv[c], lv[c]);
+          db[c] = __fadd_rn(db[c], gv);
+#pragma unroll
+          for (int j = 0; j < CP; ++j)
+            if (j < C) dw[c][j] = fmaf(a[u][c], gr[j], dw[c][j]);
+        }
+        const int64_t idx = (c0 + r + u) * H + n0;
+        if (COLS == 2) {
+          *reinterpret_cast<float2*>(dz_hi + idx) = make_float2(hv[0], hv[COLS - 1]);
+          *reinterpret_cast<float2*>(dz_lo + idx) = make_float2(lv[0], lv[COLS - 1]);
+        } else {
+          dz_hi[idx] = hv[0];
+          dz_lo[idx] = lv[0];
+        }
       }
     }
   }
   if (!active) return;
 #pragma unroll
-  for (int j = 0; j < HEAD_MAX_CLASSES; ++j)
-    if (j < C) part[((int64_t)blockIdx.y * C + j) * H + n] = dw[j];
+  for (int c = 0; c < COLS; ++c) {
+#pragma unroll
+    for (int j = 0; j < CP; ++j)
+      if (j < C) part[((int64_t)blockIdx.y * C + j) * H + n0 + c] = dw[c][j];
+    if (db_part) db_part[(int64_t)blockIdx.y * H + n0 + c] = db[c];
+  }
 }
 
+// dW[n, j] (and db[n] when db_part is given) = the row-block partials summed
+// in row-block order.
 __global__ void __launch_bounds__(256)
 dw_reduce_kernel(int64_t H, int C, int64_t row_blocks, const float* __restrict__ part,
-                 float* __restrict__ dw) {
+                 float* __restrict__ dw, const float* __restrict__ db_part,
+                 float* __restrict__ db) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= H * C) return;
-  const int64_t n = i % H;
-  const int j = (int)(i / H);
-  float s = 0.0f;
-  for (int64_t rb = 0; rb < row_blocks; ++rb) s = __fadd_rn(s, part[(rb * C + j) * H + n]);
-  dw[n * C + j] = s;
+  if (i < H * C) {
+    const int64_t n = i % H;
+    const int j = (int)(i / H);
+    float s = 0.0f;
+    for (int64_t rb = 0; rb < row_blocks; ++rb) s = __fadd_rn(s, part[(rb * C + j) * H + n]);
+    dw[n * C + j] = s;
+  } else if (db_part && i < H * C + H) {
+    const int64_t n = i - H * C;
+    float s = 0.0f;
+    for (int64_t rb = 0; rb < row_blocks; ++rb) s = __fadd_rn(s, db_part[rb * H + n]);
+    db[n] = s;
+  }
 }
 }  // namespace head
 
@@ -1348,19 +1396,48 @@ int64_t head_row_blocks(int64_t B) {
   return std::max<int64_t>(1, std::min<int64_t>(head::MAX_ROW_BLOCKS, cdiv(B, head::ROW_CHUNK)));
 }
 
-int64_t head_part_floats(int64_t B, int64_t H, int C) { return head_row_blocks(B) * C * H; }
+int64_t head_part_floats(int64_t B, int64_t H, int C) {
+  return head_row_blocks(B) * (C + 1) * H;   // dW partials, then db partials
+}
+
+template <int CP>
+static void launch_head_bwd(orca_ctx* ctx, int64_t B, int64_t H, int C, int64_t rows, int64_t rb,
+                            const float* g, const float* act_hi, const float* act_lo,
+                            const float* w_hi, const float* w_lo, float* dz_hi, float* dz_lo,
+                            float* part, float* db_part) {
+  if (H % 2 == 0) {
+    dim3 grid((unsigned)cdiv(H, 2 * head::THREADS), (unsigned)rb);
+    head::bwd_kernel<CP, 2><<<grid, head::THREADS, 0, ctx->stream>>>(
+        B, H, C, rows, g, act_hi, act_lo, w_hi, w_lo, dz_hi, dz_lo, part, db_part);
+  } else {
+    dim3 grid((unsigned)cdiv(H, head::THREADS), (unsigned)rb);
+    head::bwd_kernel<CP, 1><<<grid, head::THREADS, 0, ctx->stream>>>(
+        B, H, C, rows, g, act_hi, act_lo, w_hi, w_lo, dz_hi, dz_lo, part, db_part);
+  }
+}
 
 orca_status head_backward(orca_ctx* ctx, int64_t B, int64_t H, int C, const float* g,
                           const float* act_hi, const float* act_lo, const float* w_hi,
-                          const float* w_lo, float* dz_hi, float* dz_lo, float* part, float* dw) {
+                          const float* w_lo, float* dz_hi, float* dz_lo, float* part, float* dw,
+                          float* db) {
   if (C < 1 || C > HEAD_MAX_CLASSES) return fail(ORCA_INVALID_ARGUMENT, "head_backward: C");
   if (B <= 0 || H <= 0) return ORCA_OK;
   const int64_t rb = head_row_blocks(B);
   const int64_t rows = cdiv(B, rb);
-  dim3 grid((unsigned)cdiv(H, head::THREADS), (unsigned)rb);
-  head::bwd_kernel<<<grid, head::THREADS, 0, ctx->stream>>>(B, H, C, rows, g, act_hi, act_lo, w_hi,
-                                                            w_lo, dz_hi, dz_lo, part);
-  head::dw_reduce_kernel<<<(unsigned)cdiv(H * C, 256), 256, 0, ctx->stream>>>(H, C, rb, part, dw);
+  float* db_part = db ? part + rb * C * H : nullptr;
+#define HEAD_BWD(CP)                                                                          \
+  launch_head_bwd<CP>(ctx, B, H, C, rows, rb, g, act_hi, act_lo, w_hi, w_lo, dz_hi, dz_lo, part, \
+                      db_part)
+  switch ((C + 3) / 4) {
+    case 1: HEAD_BWD(4); break;
+    case 2: HEAD_BWD(8); break;
+    case 3: HEAD_BWD(12); break;
+    default: HEAD_BWD(16); break;
+  }
+#undef HEAD_BWD
+  const int64_t outs = H * C + (db ? H : 0);
+  head::dw_reduce_kernel<<<(unsigned)cdiv(outs, 256), 256, 0, ctx->stream>>>(H, C, rb, part, dw,
+                                                                              db_part, db);
   count_launch(ctx, 2);
   ORCA_CUDA_TRY(cudaGetLastError());
   return ORCA_OK;

@@ -95,8 +95,9 @@ orca_status head_logits(orca_ctx* ctx, const float* part, int64_t slices, int64_
 // head_backward: from g = dlogits [B, C] (plain fp32), the layer input
 // act = (act_hi + act_lo) [B, H] and W = (w_hi + w_lo) [H, C], in one pass
 // over act: dZ[m, n] = act > 0 ? sum_j g[m, j] W[n, j] : 0 written as planes,
-// and dW[n, j] = sum_m act[m, n] g[m, j] (row blocks summed in order through
-// `part`, which needs head_part_floats(B, H, C) floats).
+// dW[n, j] = sum_m act[m, n] g[m, j] and, when db is given, the bias gradient
+// of the layer below db[n] = sum_m dZ[m, n] (row blocks summed in order
+// through `part`, which needs head_part_floats(B, H, C) floats).
 // W_packed[n * 16 + j] = (w_hi + w_lo)[n * C + j] for j < C, 0 for C <= j < 16:
 // the classifier weights in the layout the next-layer dot reads.
 orca_status head_pack_weights(orca_ctx* ctx, const float* w_hi, const float* w_lo, int64_t H,
@@ -105,7 +106,8 @@ int64_t head_row_blocks(int64_t B);
 int64_t head_part_floats(int64_t B, int64_t H, int C);
 orca_status head_backward(orca_ctx* ctx, int64_t B, int64_t H, int C, const float* g,
                           const float* act_hi, const float* act_lo, const float* w_hi,
-                          const float* w_lo, float* dz_hi, float* dz_lo, float* part, float* dw);
+                          const float* w_lo, float* dz_hi, float* dz_lo, float* part, float* dw,
+                          float* db = nullptr);
 
 // Split a plain fp32 array into (hi, lo) planes: n elements.
 orca_status split_planes(orca_ctx* ctx, const float* x, float* hi, float* lo, int64_t n);

@@ -850,17 +850,23 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
   for (int l = L - 1; l >= 0; --l) {
     const int64_t K = m->dims[l], N = m->dims[l + 1];
     // db = sum over the batch (ExpandBackward -> sum_to_shape [B,N] -> [1,N]).
-    int pr = prof_open(m, "colsum_l" + std::to_string(l), (double)B * N,
-                       4.0 * ((g_lo ? 2 : 1) * B * N + N));
-    ORCA_TRY(colsum(ctx, g_hi, g_lo, B, N, g_ld, m->grads + m->p_off[2 * l + 1], m->colsum_part));
-    prof_close(m, pr);
+    int pr = -1;
+    if (!(m->use_head && l == L - 2)) {   // the classifier pass already summed this dZ
+      pr = prof_open(m, "colsum_l" + std::to_string(l), (double)B * N,
+                     4.0 * ((g_lo ? 2 : 1) * B * N + N));
+      ORCA_TRY(colsum(ctx, g_hi, g_lo, B, N, g_ld, m->grads + m->p_off[2 * l + 1],
+                      m->colsum_part));
+      prof_close(m, pr);
+    }
     if (m->use_head && l == L - 1) {
       // dW and dX of the classifier layer in one pass over its input.
       pr = prof_open(m, "head_bwd_l" + std::to_string(l), 4.0 * B * N * K,
                      4.0 * (2 * B * K + B * N + 2 * K * N + 2 * B * K + K * N));
+      // ... and the bias gradient of layer l - 1 (the column sums of its dZ).
       ORCA_TRY(head_backward(ctx, B, K, (int)N, g_hi, m->act_planes[l], m->act_planes[l] + B * K,
                              m->w_hi[l], m->w_lo[l], m->dz[cur], m->dz[cur] + B * K,
-                             m->head_part, m->grads + m->p_off[2 * l]));
+                             m->head_part, m->grads + m->p_off[2 * l],
+                             m->grads + m->p_off[2 * (l - 1) + 1]));
       prof_close(m, pr);
       if (m->comm) ORCA_TRY(launch_layer_allreduce(m, l));
       g_hi = m->dz[cur];

@@ -118,11 +118,14 @@ def test_first_step_gradients_match_oracle(be, path):
 
 
 @pytest.mark.parametrize("dims,B", [([784, 300, 200, 7], 200), ([64, 136, 1000, 16], 96),
-                                    ([784, 512, 256, 10], 256), ([32, 64, 64, 17], 64)])
+                                    ([784, 512, 256, 10], 256), ([32, 64, 64, 17], 64),
+                                    ([64, 96, 75, 3], 300)])
 def test_classifier_head_fusion(be, dims, B):
     """The classifier layer (C <= 16) on the tensor-core path: logits from the
     last hidden GEMM's epilogue (ragged 128-column slices, C not a multiple of
-    4, C = 16) and dW/dX in one pass; C = 17 takes the plain products.  Loss,
+    4, C = 16) and dW/dX plus the bias gradient of the layer below in one pass
+    (two columns per thread; an odd hidden width takes the one-column variant
+    and the plain forward product); C = 17 takes the plain products.  Loss,
     logits and every gradient of one step against the oracle."""
     x, t, _ = make_batch(dims, B, 5)
     tr = make(be, dims, B, "sgd", "tc", lr=0.0)
