@@ -260,7 +260,8 @@ struct orca_mlp {
   float* state0 = nullptr;           // SGD velocity / AdamW m (same layout as grads)
   float* state1 = nullptr;           // AdamW v
   // activations
-  float* x_planes = nullptr;         // [2][B][dims[0]]
+  float* x_planes = nullptr;         // [2][B][x_ld]: input planes + a column of ones
+  int64_t x_ld = 0;                  // dims[0] + 1 rounded up to a multiple of 4
   std::vector<float*> act_planes;    // act_planes[l] = [2][B][dims[l]], l = 1..L-1
   float* t_buf = nullptr;            // one-hot target [B][C]
   float* x_stage = nullptr;          // raw input [B][dims[0]]
@@ -348,6 +349,31 @@ static orca_status mlp_alloc(orca_mlp* m, void** p, size_t bytes) {
 }
 
 static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad);
+
+// Input planes: x [B][D] -> hi, lo [B][x_ld] with column D = 1 (hi) / 0 (lo)
+// and zeros after it (see the dW product of layer 0).
+__global__ void split_input_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                   float* __restrict__ lo, int64_t B, int64_t D, int64_t ld) {
+  const int64_t n = B * ld;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / ld, c = i % ld;
+    float h = c == D ? 1.0f : 0.0f, l = 0.0f;
+    if (c < D) split_tf32(x[r * D + c], h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+static orca_status split_input(orca_mlp* m, const float* x) {
+  const int64_t n = m->B * m->x_ld;
+  const int blocks = (int)std::min<int64_t>(cdiv(n, 256), (int64_t)m->ctx->sm_count * 8);
+  split_input_kernel<<<blocks, 256, 0, m->ctx->stream>>>(x, m->x_planes, m->x_planes + n, m->B,
+                                                         m->dims[0], m->x_ld);
+  count_launch(m->ctx);
+  ORCA_CUDA_TRY(cudaGetLastError());
+  return ORCA_OK;
+}
 static orca_status mlp_backward_impl(orca_mlp* m);
 static orca_status mlp_update_impl(orca_mlp* m);
 
@@ -449,7 +475,8 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
   if (m->opt == ORCA_OPT_ADAMW) ALLOC(state1, pbytes);
   if (m->state0) cudaMemset(m->state0, 0, pbytes);
   if (m->state1) cudaMemset(m->state1, 0, pbytes);
-  ALLOC(x_planes, (size_t)(2 * B * m->dims[0]) * 4);
+  m->x_ld = (m->dims[0] + 1 + 3) / 4 * 4;
+  ALLOC(x_planes, (size_t)(2 * B * m->x_ld) * 4);
   ALLOC(x_stage, (size_t)(B * m->dims[0]) * 4);
   ALLOC(t_buf, (size_t)(B * C) * 4);
   ALLOC(logits, (size_t)(B * C) * 4);
@@ -595,7 +622,7 @@ static orca_status step_device_locked(orca_mlp* m, const float* x_dev, const flo
   const uint64_t l0 = ctx->launches.load();
   const int64_t B = m->B, C = m->dims[m->L];
   const int pr = prof_open(m, "split_input", 0.0, 12.0 * B * m->dims[0]);
-  ORCA_TRY(split_planes(ctx, x_dev, m->x_planes, m->x_planes + B * m->dims[0], B * m->dims[0]));
+  ORCA_TRY(split_input(m, x_dev));
   prof_close(m, pr);
   if (t_dev != m->t_buf)
     ORCA_CUDA_TRY(cudaMemcpyAsync(m->t_buf, t_dev, (size_t)(B * C) * 4, cudaMemcpyDeviceToDevice,
@@ -653,8 +680,7 @@ orca_status orca_mlp_forward(orca_mlp* m, const float* x, const float* t, float*
   const int64_t B = m->B, C = m->dims[m->L];
   ORCA_CUDA_TRY(cudaMemcpyAsync(m->x_stage, x, (size_t)(B * m->dims[0]) * 4,
                                 cudaMemcpyHostToDevice, ctx->stream));
-  ORCA_TRY(split_planes(ctx, m->x_stage, m->x_planes, m->x_planes + B * m->dims[0],
-                        B * m->dims[0]));
+  ORCA_TRY(split_input(m, m->x_stage));
   if (t) {
     ORCA_CUDA_TRY(cudaMemcpyAsync(m->t_buf, t, (size_t)(B * C) * 4, cudaMemcpyHostToDevice,
                                   ctx->stream));
@@ -733,8 +759,8 @@ static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad) {
     const int64_t K = m->dims[l], N = m->dims[l + 1];
     Operand a, w;
     a.hi = l == 0 ? m->x_planes : m->act_planes[l];
-    a.lo = a.hi + B * K;
-    a.ld = K;
+    a.ld = l == 0 ? m->x_ld : K;
+    a.lo = a.hi + B * a.ld;
     a.mn_major = false;
     w.hi = m->w_hi[l];
     w.lo = m->w_lo[l];
@@ -851,7 +877,9 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
     const int64_t K = m->dims[l], N = m->dims[l + 1];
     // db = sum over the batch (ExpandBackward -> sum_to_shape [B,N] -> [1,N]).
     int pr = -1;
-    if (!(m->use_head && l == L - 2)) {   // the classifier pass already summed this dZ
+    // The classifier pass already summed the dZ of layer L - 2, and layer 0's
+    // bias gradient comes out of its dW product (the input's column of ones).
+    if (!(m->use_head && l == L - 2) && l != 0) {
       pr = prof_open(m, "colsum_l" + std::to_string(l), (double)B * N,
                      4.0 * ((g_lo ? 2 : 1) * B * N + N));
       ORCA_TRY(colsum(ctx, g_hi, g_lo, B, N, g_ld, m->grads + m->p_off[2 * l + 1],
@@ -875,12 +903,16 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
       cur ^= 1;
       continue;
     }
-    // dW = act^T @ g : M = K (features), N, K_gemm = B.
+    // dW = act^T @ g : M = K (features), N, K_gemm = B.  For layer 0 the
+    // input planes carry a column of ones after the K features, so the
+    // product has K + 1 rows and its last row, sum_m g[m, :], is db0 -- which
+    // the arena stores right after dW0.
     Operand at, g;
     at.hi = l == 0 ? m->x_planes : m->act_planes[l];
-    at.lo = at.hi + B * K;
-    at.ld = K;
+    at.ld = l == 0 ? m->x_ld : K;
+    at.lo = at.hi + B * at.ld;
     at.mn_major = true;
+    const int64_t dw_rows = l == 0 ? K + 1 : K;
     g.hi = g_hi;
     g.lo = g_lo;
     g.ld = g_ld;
@@ -891,8 +923,9 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
     ew.ldc = N;
     pr = prof_open(m, "gemm_dw_l" + std::to_string(l), 2.0 * B * N * K,
                    4.0 * (2 * B * K + (g_lo ? 2 : 1) * B * N + K * N),
-                   gemm_select(ctx, K, N, B, at, g, ew, m->gemm_path));
-    ORCA_TRY(gemm(ctx, K, N, B, at, g, ew, m->gemm_path, m->workspace, m->workspace_bytes));
+                   gemm_select(ctx, dw_rows, N, B, at, g, ew, m->gemm_path));
+    ORCA_TRY(gemm(ctx, dw_rows, N, B, at, g, ew, m->gemm_path, m->workspace,
+                  m->workspace_bytes));
     prof_close(m, pr);
     if (m->comm) ORCA_TRY(launch_layer_allreduce(m, l));
     if (l == 0) break;
