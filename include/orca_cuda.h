@@ -206,6 +206,15 @@ orca_status orca_scatter(orca_ctx* ctx, const orca_buf* x, int64_t dim, const or
 orca_status orca_linear_fwd(orca_ctx* ctx, const orca_buf* x, const orca_buf* w,
                             const orca_buf* b, int64_t m, int64_t k, int64_t n, int relu,
                             orca_buf** out);
+/* Backward of out = x @ w + b, fused (MatMulBackward + ExpandBackward,
+ * orca-autograd/src/backend.rs:1448-1499 and 1675-1698): dW = x^T dy [k,n],
+ * db = the row sum of dy [1,n], and, when dx is not null, dX = dy w^T [m,k]
+ * masked by (mask > 0) when mask is given — the ReluBackward of the layer
+ * below (backend.rs:1624-1646; mask = that layer's pre-activation or
+ * activation).  x [m,k], w [k,n] ([in,out]), dy [m,n]; F32 only. */
+orca_status orca_linear_bwd(orca_ctx* ctx, const orca_buf* x, const orca_buf* w,
+                            const orca_buf* dy, const orca_buf* mask, int64_t m, int64_t k,
+                            int64_t n, orca_buf** dx, orca_buf** dw, orca_buf** db);
 /* C[m,n] = op(A) @ op(B) on plain f32 buffers, FP32-accurate.  a_mn_major /
  * b_mn_major select the storage of A ([k,m] instead of [m,k]) and B ([k,n]
  * row-major, the reference's [in,out] layout, vs [n,k]), i.e. X@W, dY@W^T and

@@ -231,6 +231,16 @@ class CudaBackend:
         return self._out(L.load().orca_linear_fwd, x._h, w._h, b._h if b is not None else None,
                          int(m), int(k), int(n), 1 if relu else 0)
 
+    def linear_bwd(self, x, w, dy, m, k, n, mask=None, need_dx=True):
+        """(dx or None, dw, db) of out = x @ w + b; dx masked by mask > 0."""
+        dx, dw, db = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        L.check(L.load().orca_linear_bwd(self._ctx, x._h, w._h, dy._h,
+                                         mask._h if mask is not None else None, int(m), int(k),
+                                         int(n), ctypes.byref(dx) if need_dx else None,
+                                         ctypes.byref(dw), ctypes.byref(db)))
+        return (CudaStorage(dx, self) if need_dx else None, CudaStorage(dw, self),
+                CudaStorage(db, self))
+
     def gemm_ex(self, m, n, k, a, a_mn_major, b, b_mn_major, path=0):
         return self._out(L.load().orca_gemm_ex, int(m), int(n), int(k), a._h,
                          1 if a_mn_major else 0, b._h, 1 if b_mn_major else 0, int(path))

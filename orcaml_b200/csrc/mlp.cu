@@ -226,6 +226,13 @@ static int ew_grid(orca_ctx* ctx, int64_t n) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), (int64_t)ctx->sm_count * 8));
 }
 
+// g[i] = mask[i] > 0 ? g[i] : 0 (one comparison, no arithmetic: bit-exact).
+__global__ void mask_kernel(float* __restrict__ g, const float* __restrict__ mask, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    if (!(mask[i] > 0.0f)) g[i] = 0.0f;
+}
+
 orca_status colsum(orca_ctx* ctx, const float* hi, const float* lo, int64_t B, int64_t N,
                    int64_t ld, float* out, float* part) {
   const int chunks = (int)cdiv(B, COLSUM_ROWS);
@@ -1063,6 +1070,79 @@ orca_status orca_linear_fwd(orca_ctx* ctx, const orca_buf* x, const orca_buf* w,
     count_launch(ctx);
   }
   cudaFreeAsync(scratch, ctx->stream);
+  return s;
+}
+
+orca_status orca_linear_bwd(orca_ctx* ctx, const orca_buf* x, const orca_buf* w, const orca_buf* dy,
+                            const orca_buf* mask, int64_t m, int64_t k, int64_t n, orca_buf** dx,
+                            orca_buf** dw, orca_buf** db) {
+  ORCA_TRY(check_ctx(ctx));
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  if (!x || !w || !dy || !dw || !db) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (m < 1 || k < 1 || n < 1) return fail(ORCA_INVALID_ARGUMENT, "linear_bwd: empty shape");
+  if (x->n < (size_t)(m * k) || w->n < (size_t)(k * n) || dy->n < (size_t)(m * n) ||
+      (mask && mask->n < (size_t)(m * k)))
+    return fail(ORCA_SHAPE_MISMATCH, "linear_bwd: buffer sizes");
+  for (const orca_buf* b : {x, w, dy, mask})
+    if (b && b->dtype != ORCA_F32) return fail(ORCA_UNSUPPORTED_DTYPE, "linear_bwd: F32 only");
+  if (dx) *dx = nullptr;
+  *dw = *db = nullptr;
+  ORCA_TRY(new_buf(ctx, (size_t)(k * n), ORCA_F32, dw));
+  orca_status s = new_buf(ctx, (size_t)n, ORCA_F32, db);
+  if (s == ORCA_OK && dx) s = new_buf(ctx, (size_t)(m * k), ORCA_F32, dx);
+  float* scratch = nullptr;
+  const size_t elems = 2 * (size_t)(m * k) + 2 * (size_t)(k * n) + 2 * (size_t)(m * n) +
+                       (size_t)(cdiv(m, COLSUM_ROWS) * n);
+  if (s == ORCA_OK &&
+      cudaMallocAsync(reinterpret_cast<void**>(&scratch), elems * 4, ctx->stream) != cudaSuccess)
+    s = fail(ORCA_CUDA_ERROR, "linear_bwd: scratch allocation failed");
+  if (s == ORCA_OK) {
+    float* xh = scratch;
+    float* wh = xh + 2 * m * k;
+    float* gh = wh + 2 * k * n;
+    float* part = gh + 2 * m * n;
+    s = split_planes(ctx, (const float*)x->ptr, xh, xh + m * k, m * k);
+    if (s == ORCA_OK) s = split_planes(ctx, (const float*)w->ptr, wh, wh + k * n, k * n);
+    if (s == ORCA_OK) s = split_planes(ctx, (const float*)dy->ptr, gh, gh + m * n, m * n);
+    // dW = x^T dy (MatMulBackward, orca-autograd/src/backend.rs:1448-1499).
+    Operand at, g;
+    at.hi = xh; at.lo = xh + m * k; at.ld = k; at.mn_major = true;
+    g.hi = gh; g.lo = gh + m * n; g.ld = n; g.mn_major = true;
+    Epilogue ew;
+    ew.mode = EPI_STORE;
+    ew.out = (float*)(*dw)->ptr;
+    ew.ldc = n;
+    if (s == ORCA_OK) s = gemm(ctx, k, n, m, at, g, ew, GEMM_AUTO);
+    // db = sum over rows of dy (ExpandBackward -> sum_to_shape, backend.rs:1675-1698).
+    if (s == ORCA_OK) s = colsum(ctx, (const float*)dy->ptr, nullptr, m, n, n,
+                                 (float*)(*db)->ptr, part);
+    if (s == ORCA_OK && dx) {
+      // dX = dy W^T, then the ReLU mask of the layer below (ReluBackward,
+      // backend.rs:1624-1646: the gradient passes where the input was > 0).
+      Operand ga, wt;
+      ga.hi = gh; ga.lo = gh + m * n; ga.ld = n;
+      wt.hi = wh; wt.lo = wh + k * n; wt.ld = n;
+      Epilogue ex;
+      ex.mode = EPI_STORE;
+      ex.out = (float*)(*dx)->ptr;
+      ex.ldc = k;
+      s = gemm(ctx, m, k, n, ga, wt, ex, GEMM_AUTO);
+      if (s == ORCA_OK && mask) {
+        mask_kernel<<<ew_grid(ctx, m * k), 256, 0, ctx->stream>>>(
+            (float*)(*dx)->ptr, (const float*)mask->ptr, m * k);
+        count_launch(ctx);
+        if (cudaGetLastError() != cudaSuccess) s = fail(ORCA_CUDA_ERROR, "linear_bwd: mask");
+      }
+    }
+    cudaFreeAsync(scratch, ctx->stream);
+  }
+  if (s != ORCA_OK) {
+    for (orca_buf** o : {dx, dw, db})
+      if (o && *o) {
+        orca_buf_release(*o);
+        *o = nullptr;
+      }
+  }
   return s;
 }
 

@@ -120,3 +120,31 @@ def test_linear_fwd_bias_relu(be):
     ref = np.maximum(z, 0)
     scale = np.abs(x).astype(np.float64) @ np.abs(w).astype(np.float64) + np.abs(bias)
     assert np.all(np.abs(out.reshape(m, n) - ref) <= 1e-5 * scale + 1e-30)
+
+
+@pytest.mark.parametrize("m,k,n,with_mask", [(300, 784, 512, True), (64, 100, 10, True),
+                                             (2048, 512, 1024, False), (7, 5, 3, True)])
+def test_linear_bwd_fused(be, m, k, n, with_mask):
+    """orca_linear_bwd: dW = x^T dy, db = row sum of dy, dX = dy W^T masked by
+    mask > 0, against float64 (FP32-accuracy bound of each product)."""
+    x = RNG.standard_normal((m, k)).astype(np.float32)
+    w = (RNG.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    dy = RNG.standard_normal((m, n)).astype(np.float32)
+    mask = RNG.standard_normal((m, k)).astype(np.float32) if with_mask else None
+    up = lambda a: be.from_f32_slice([a.size], a)
+    dx, dw, db = be.linear_bwd(up(x), up(w), up(dy), m, k, n,
+                               mask=up(mask) if with_mask else None)
+    assert_fp32_gemm(be.to_f32_vec(dw).reshape(k, n), x.T, dy)
+    ref_db = dy.astype(np.float64).sum(axis=0)
+    assert np.all(np.abs(be.to_f32_vec(db) - ref_db) <= 1e-5 * np.abs(dy).astype(np.float64).sum(0))
+    got_dx = be.to_f32_vec(dx).reshape(m, k)
+    ref = dy.astype(np.float64) @ w.astype(np.float64).T
+    scale = np.abs(dy).astype(np.float64) @ np.abs(w).astype(np.float64).T
+    if with_mask:
+        keep = mask > 0
+        assert np.all(got_dx[~keep] == 0)
+        assert np.all(np.abs(got_dx - ref)[keep] <= 1e-5 * scale[keep] + 1e-30)
+    else:
+        assert np.all(np.abs(got_dx - ref) <= 1e-5 * scale + 1e-30)
+    _, dw2, _ = be.linear_bwd(up(x), up(w), up(dy), m, k, n, need_dx=False)
+    assert np.array_equal(be.to_f32_vec(dw2), be.to_f32_vec(dw))
