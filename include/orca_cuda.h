@@ -286,6 +286,18 @@ orca_status orca_mlp_set_param(orca_mlp* mlp, int index, const float* host, int6
 orca_status orca_mlp_get_param(orca_mlp* mlp, int index, float* host, int64_t numel);
 /* Gradient of the last backward (after the all-reduce when a comm is attached). */
 orca_status orca_mlp_get_grad(orca_mlp* mlp, int index, float* host, int64_t numel);
+/* Optimizer state of parameter `index` for checkpoints (the reference's
+ * optimizers keep it in Python objects and never save it, optim/sgd.py:46-79,
+ * adamw.py:48-99): slot 0 = SGD velocity / AdamW first moment m, slot 1 =
+ * AdamW second moment v.  *numel = 0 when the optimizer has no such slot. */
+orca_status orca_mlp_state_numel(const orca_mlp* mlp, int slot, int index, int64_t* numel);
+orca_status orca_mlp_get_state(orca_mlp* mlp, int slot, int index, float* host, int64_t numel);
+orca_status orca_mlp_set_state(orca_mlp* mlp, int slot, int index, const float* host,
+                               int64_t numel);
+/* Step counters: AdamW's t (bias correction) and whether SGD's velocity holds a
+ * value (the first momentum step sets v = g, sgd.py:67-71). */
+orca_status orca_mlp_get_step(const orca_mlp* mlp, int64_t* t, int* velocity_started);
+orca_status orca_mlp_set_step(orca_mlp* mlp, int64_t t, int velocity_started);
 /* Attach (or detach with NULL) the communicator used by every later step. */
 orca_status orca_mlp_attach_comm(orca_mlp* mlp, orca_comm* comm, size_t bucket_bytes);
 /* One training step with host inputs: x [batch, dims[0]] and the one-hot (or

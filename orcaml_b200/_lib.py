@@ -101,6 +101,11 @@ _SIGS = {
                      PP], c_int),
     "orca_scatter": ([c_void_p, c_void_p, c_int64, c_void_p, c_void_p, P_int64, c_int, P_int64,
                       c_int, c_int, PP], c_int),
+    "orca_mlp_state_numel": ([c_void_p, c_int, c_int, P_int64], c_int),
+    "orca_mlp_get_state": ([c_void_p, c_int, c_int, c_void_p, c_int64], c_int),
+    "orca_mlp_set_state": ([c_void_p, c_int, c_int, c_void_p, c_int64], c_int),
+    "orca_mlp_get_step": ([c_void_p, P_int64, ctypes.POINTER(c_int)], c_int),
+    "orca_mlp_set_step": ([c_void_p, c_int64, c_int], c_int),
     "orca_linear_bwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                          c_int64, PP, PP, PP], c_int),
     "orca_linear_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,

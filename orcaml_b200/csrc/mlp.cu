@@ -616,6 +616,56 @@ orca_status orca_mlp_get_grad(orca_mlp* m, int index, float* host, int64_t numel
   return check_device_error(m->ctx);
 }
 
+orca_status orca_mlp_state_numel(const orca_mlp* m, int slot, int index, int64_t* numel) {
+  if (!m || !numel || slot < 0 || slot > 1) return fail(ORCA_INVALID_ARGUMENT, "bad state slot");
+  int64_t n;
+  ORCA_TRY(orca_mlp_param_numel(m, index, &n));
+  const float* base = slot == 0 ? m->state0 : m->state1;
+  *numel = base ? n : 0;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_get_state(orca_mlp* m, int slot, int index, float* host, int64_t numel) {
+  int64_t n;
+  ORCA_TRY(orca_mlp_state_numel(m, slot, index, &n));
+  if (n == 0 || n != numel || !host) return fail(ORCA_SHAPE_MISMATCH, "get_state: size");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  const float* base = slot == 0 ? m->state0 : m->state1;
+  ORCA_TRY(finish_sync(m));
+  ORCA_TRY(copy_to_host(m->ctx, host, base + m->p_off[index], (size_t)n * 4));
+  return check_device_error(m->ctx);
+}
+
+orca_status orca_mlp_set_state(orca_mlp* m, int slot, int index, const float* host,
+                               int64_t numel) {
+  int64_t n;
+  ORCA_TRY(orca_mlp_state_numel(m, slot, index, &n));
+  if (n == 0 || n != numel || !host) return fail(ORCA_SHAPE_MISMATCH, "set_state: size");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  float* base = slot == 0 ? m->state0 : m->state1;
+  ORCA_TRY(finish_sync(m));
+  ORCA_CUDA_TRY(cudaMemcpyAsync(base + m->p_off[index], host, (size_t)n * 4,
+                                cudaMemcpyHostToDevice, m->ctx->stream));
+  return finish_sync(m);
+}
+
+orca_status orca_mlp_get_step(const orca_mlp* m, int64_t* t, int* velocity_started) {
+  if (!m || !t || !velocity_started) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  *t = m->t;
+  *velocity_started = m->vel_init ? 1 : 0;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_set_step(orca_mlp* m, int64_t t, int velocity_started) {
+  if (!m || t < 0) return fail(ORCA_INVALID_ARGUMENT, "bad step count");
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  m->t = t;
+  m->vel_init = velocity_started != 0;
+  return ORCA_OK;
+}
+
 orca_status orca_mlp_attach_comm(orca_mlp* m, orca_comm* comm, size_t bucket_bytes) {
   if (!m) return fail(ORCA_INVALID_ARGUMENT, "null mlp");
   m->comm = comm;

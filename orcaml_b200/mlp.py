@@ -19,6 +19,7 @@ from typing import List, Optional, Sequence
 import numpy as np
 
 from . import _lib as L
+from . import safetensors_io
 from .backend import CudaBackend
 
 OPT = {"sgd": 0, "adamw": 1}
@@ -133,6 +134,92 @@ class MlpTrainer:
             L.check(L.load().orca_mlp_get_grad(self._h, i, a.ctypes.data_as(ctypes.c_void_p), a.size))
             out.append(a)
         return out
+
+    # -- checkpoints (safetensors)
+    def param_names(self) -> List[str]:
+        """The keys the reference's Module.save_weights gives the same model
+        built as Sequential(Linear, ReLU, ..., Linear): modules are numbered in
+        order (nn/container.py:10-11), the ReLUs take the odd indices, and
+        Linear registers `weight` [in,out] and `bias` [1,out]
+        (nn/module.py:169-187, nn/linear.py:29-36)."""
+        out = []
+        for i in range(len(self.dims) - 1):
+            out += [f"{2 * i}.weight", f"{2 * i}.bias"]
+        return out
+
+    def save_weights(self, path: str):
+        """Parameters only, in the file format and with the keys of the
+        reference's Module.save_weights -- loadable by its load_weights."""
+        entries = {n: ("F32", list(p.shape), p.tobytes())
+                   for n, p in zip(self.param_names(), self.get_parameters())}
+        safetensors_io.write(path, entries)
+
+    def load_weights(self, path: str):
+        """Reads a file written by save_weights or by the reference's
+        Module.save_weights (keys and shapes must match this model)."""
+        entries, _ = safetensors_io.read(path)
+        params = []
+        for name, shape in zip(self.param_names(), self.param_shapes()):
+            if name not in entries:
+                raise ValueError(f"{path}: missing tensor {name!r}")
+            dtype, got, data = entries[name]
+            if dtype != "F32" or int(np.prod(got)) != shape[0] * shape[1]:
+                raise ValueError(f"{path}: {name!r} is {dtype} {got}, expected F32 {list(shape)}")
+            params.append(np.frombuffer(data, np.float32).reshape(shape))
+        self.set_parameters(params)
+
+    def _state_slots(self):
+        lib = L.load()
+        slots = []
+        for slot, suffix in ((0, "momentum_buffer" if self.optimizer == "sgd" else "exp_avg"),
+                             (1, "exp_avg_sq")):
+            n = ctypes.c_int64()
+            L.check(lib.orca_mlp_state_numel(self._h, slot, 0, ctypes.byref(n)))
+            if n.value:
+                slots.append((slot, suffix))
+        return slots
+
+    def save_checkpoint(self, path: str):
+        """Weights (as save_weights) plus the optimizer state the reference
+        does not save: per parameter `optimizer.<key>.<slot>` tensors and the
+        step counters in the file's metadata."""
+        lib = L.load()
+        entries = {n: ("F32", list(p.shape), p.tobytes())
+                   for n, p in zip(self.param_names(), self.get_parameters())}
+        for slot, suffix in self._state_slots():
+            for i, (name, shape) in enumerate(zip(self.param_names(), self.param_shapes())):
+                a = np.empty(shape, np.float32)
+                L.check(lib.orca_mlp_get_state(self._h, slot, i, a.ctypes.data_as(ctypes.c_void_p),
+                                               a.size))
+                entries[f"optimizer.{name}.{suffix}"] = ("F32", list(shape), a.tobytes())
+        t, started = ctypes.c_int64(), ctypes.c_int()
+        L.check(lib.orca_mlp_get_step(self._h, ctypes.byref(t), ctypes.byref(started)))
+        meta = {"format": "orcaml_b200.mlp", "optimizer": self.optimizer,
+                "dims": ",".join(str(d) for d in self.dims), "step": str(t.value),
+                "velocity_started": str(started.value)}
+        safetensors_io.write(path, entries, meta)
+
+    def load_checkpoint(self, path: str):
+        """Restores weights, optimizer state and step counters written by
+        save_checkpoint, so training continues bit-for-bit as if uninterrupted."""
+        lib = L.load()
+        entries, meta = safetensors_io.read(path)
+        if meta.get("optimizer") != self.optimizer or \
+                meta.get("dims") != ",".join(str(d) for d in self.dims):
+            raise ValueError(f"{path}: checkpoint of a different model or optimizer")
+        self.load_weights(path)
+        for slot, suffix in self._state_slots():
+            for i, (name, shape) in enumerate(zip(self.param_names(), self.param_shapes())):
+                key = f"optimizer.{name}.{suffix}"
+                if key not in entries:
+                    raise ValueError(f"{path}: missing optimizer state {key!r}")
+                a = np.ascontiguousarray(np.frombuffer(entries[key][2], np.float32))
+                if a.size != shape[0] * shape[1]:
+                    raise ValueError(f"{path}: {key!r} has the wrong size")
+                L.check(lib.orca_mlp_set_state(self._h, slot, i, a.ctypes.data_as(ctypes.c_void_p),
+                                               a.size))
+        L.check(lib.orca_mlp_set_step(self._h, int(meta.get("step", "0")),
+                                      int(meta.get("velocity_started", "0"))))
 
     # -- steps
     def _check_batch(self, x, t):

@@ -228,3 +228,39 @@ def test_forward_only_and_validation(be):
     with pytest.raises(ValueError):
         MlpTrainer(be, dims, B, optimizer="adamw", lr=1e-3, betas=(1.0, 0.9))
     tr.close()
+
+
+@pytest.mark.parametrize("opt", ["sgd", "adamw"])
+def test_checkpoint_resume_is_bit_identical(be, tmp_path, opt):
+    """save_checkpoint after 3 steps, load into a fresh trainer: the next 3
+    steps (losses and parameters) are bit-identical to an uninterrupted run;
+    save_weights writes the reference's Sequential keys."""
+    dims, B = [784, 256, 128, 10], 64
+    kw = dict(lr=1e-3, weight_decay=0.01) if opt == "adamw" else dict(lr=0.01, momentum=0.9)
+    x, t, _ = make_batch(dims, B, 2)
+    a = make(be, dims, B, opt, **kw)
+    for _ in range(3):
+        a.step(x, t)
+    path = str(tmp_path / "ck.safetensors")
+    a.save_checkpoint(path)
+    b = make(be, dims, B, opt, **kw)
+    b.load_checkpoint(path)
+    la = [a.step(x, t) for _ in range(3)]
+    lb = [b.step(x, t) for _ in range(3)]
+    assert la == lb
+    for p, q in zip(a.get_parameters(), b.get_parameters()):
+        assert np.array_equal(p, q)
+    wpath = str(tmp_path / "w.safetensors")
+    a.save_weights(wpath)
+    from orcaml_b200 import safetensors_io
+    entries, _ = safetensors_io.read(wpath)
+    assert sorted(entries) == ["0.bias", "0.weight", "2.bias", "2.weight", "4.bias", "4.weight"]
+    assert entries["2.weight"][1] == [256, 128] and entries["2.bias"][1] == [1, 128]
+    c = make(be, dims, B, opt, **kw)
+    c.load_weights(wpath)
+    for p, q in zip(a.get_parameters(), c.get_parameters()):
+        assert np.array_equal(p, q)
+    with pytest.raises(ValueError):
+        make(be, [784, 256, 64, 10], B, opt, **kw).load_checkpoint(path)
+    for tr in (a, b, c):
+        tr.close()
