@@ -3,6 +3,11 @@ training (SGD momentum 0.9, lr 0.01, per-rank batch
 4096) on N B200s, one process per GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c0|c1|c4]
+
+The default workload is configs[2], the configuration BASELINE's metric is
+quoted on; `--config` runs the other MLP configs the same way (their own
+optimizer, inputs and shapes) for reference measurements.
 
 A step is one full training step (forward, softmax-CE, backward, NCCL
 all-reduce of the gradients when N > 1, optimizer update).  Every rank holds a
@@ -35,8 +40,34 @@ sys.path.insert(0, REPO)
 from orcaml_b200.synthetic import CONFIGS, init_params, make_batch  # noqa: E402
 
 CFG = CONFIGS["c2"]
-METRIC = "train samples/s, MLP 784-8192-8192-10 FP32 DDP (SGD momentum 0.9, per-rank batch 4096)"
+METRIC_C2 = "train samples/s, MLP 784-8192-8192-10 FP32 DDP (SGD momentum 0.9, per-rank batch 4096)"
+METRIC = METRIC_C2
 UNIT = "samples/s"
+
+
+def opt_kwargs(cfg):
+    if cfg.optimizer == "adamw":
+        return dict(lr=cfg.lr, weight_decay=cfg.weight_decay, betas=cfg.betas, eps=cfg.eps)
+    return dict(lr=cfg.lr, momentum=cfg.momentum, dampening=cfg.dampening,
+                weight_decay=cfg.weight_decay)
+
+
+def describe(cfg):
+    """'BASELINE configs[i]: MLP ..., optimizer ..., per-rank batch B'."""
+    dims = "-".join(str(d) for d in cfg.dims)
+    if cfg.optimizer == "adamw":
+        opt = f"AdamW lr {cfg.lr:g} wd {cfg.weight_decay:g}"
+    else:
+        opt = f"SGD momentum {cfg.momentum:g} lr {cfg.lr:g}" if cfg.momentum else f"SGD lr {cfg.lr:g}"
+    return f"BASELINE configs[{cfg.name[1:]}]: MLP {dims}, {opt}, per-rank batch {cfg.batch}"
+
+
+def set_config(name):
+    global CFG, METRIC
+    CFG = CONFIGS[name]
+    METRIC = METRIC_C2 if name == "c2" else (
+        f"train samples/s, MLP {'-'.join(str(d) for d in CFG.dims)} FP32 DDP "
+        f"({describe(CFG).split(', ', 1)[1]})")
 
 
 def load_peaks():
@@ -110,9 +141,10 @@ def cpu_baseline(steps=1, batch=64, warmup=0):
     from oracle import oracle as O
     O.set_threads(0)
     dims = CFG.dims
-    tr = O.OracleTrainer(dims, init_params(dims, 1), optimizer="sgd", lr=CFG.lr,
-                         momentum=CFG.momentum)
-    x, t, _ = make_batch(dims, batch, 0)
+    kw = opt_kwargs(CFG)
+    kw.pop("betas", None), kw.pop("eps", None)
+    tr = O.OracleTrainer(dims, init_params(dims, 1), optimizer=CFG.optimizer, **kw)
+    x, t, _ = make_batch(dims, batch, 0, CFG.inputs)
     for _ in range(warmup):
         tr.step(x, t)
     t0 = time.perf_counter()
@@ -121,8 +153,9 @@ def cpu_baseline(steps=1, batch=64, warmup=0):
     dt = time.perf_counter() - t0
     return {"value": steps * batch / dt, "unit": UNIT, "cores": O.threads(),
             "kind": "port",
-            "sample": f"{steps} step(s) of the 784-8192-8192-10 SGD-momentum step at batch {batch} "
-                      f"(of 4096): GEMM single-threaded, element-wise loops on {O.threads()} threads",
+            "sample": f"{steps} step(s) of the {'-'.join(str(d) for d in dims)} {CFG.optimizer} "
+                      f"step at batch {batch} (of {CFG.batch}): GEMM single-threaded, element-wise "
+                      f"loops on {O.threads()} threads",
             "seconds": dt}
 
 
@@ -145,8 +178,8 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * res["seconds"] / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "784-8192-8192-10 SGD momentum 0.9 step, CPU, "
-                                   f"bounded sample of {batch} rows per step",
+            "config": {"workload": describe(CFG) + f"; CPU, bounded sample of {batch} rows "
+                                                   "per step",
                        "global_batch": batch, "parallelism": "single process (rank 0)"},
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -172,7 +205,7 @@ def run_ours(args):
 
     be = CudaBackend(local)
     B = CFG.batch
-    tr = MlpTrainer(be, CFG.dims, B, optimizer="sgd", lr=CFG.lr, momentum=CFG.momentum)
+    tr = MlpTrainer(be, CFG.dims, B, optimizer=CFG.optimizer, **opt_kwargs(CFG))
     tr.set_parameters(init_params(CFG.dims, 1))
     comm = None
     if world > 1:
@@ -181,7 +214,7 @@ def run_ours(args):
         comm = NcclCommunicator(be, rank, world, obj[0], timeout=120.0)
         tr.attach_comm(comm, bucket_bytes=args.bucket_mb << 20)
 
-    x, t, _ = make_batch(CFG.dims, B, rank)
+    x, t, _ = make_batch(CFG.dims, B, rank, CFG.inputs)
     xs = be.from_f32_slice(list(x.shape), x)
     ts = be.from_f32_slice(list(t.shape), t)
     loss_s = be.zeros([1])
@@ -251,35 +284,43 @@ def run_ours(args):
     tc_ms = sum(s["ms"] for s in tc_sites)
     tc_flops = sum(s["flops"] * s["launches"] for s in tc_sites)
     tc_launches = sum(s["launches"] for s in tc_sites)
-    # DRAM read + write of one tc_gemm_kernel launch, from an ncu --set full
-    # capture of the forward layer-2 GEMM (M=4096, N=8192, K=8192): 2.908 GB
-    # read + 0.240 GB written; its algorithmic operand + output bytes are 1.07 GB.
-    traffic = {"bytes_per_launch": 3.148e9, "launch": "forward layer 2, 4096x8192x8192",
-               "algorithmic_bytes": 1.074e9}
+    # DRAM read + write of one tcgen05 GEMM launch, from an ncu --set full
+    # capture (profiles/tc_gemm_kdot_c2_fwd_l1.md) of the configs[2] forward
+    # product of the 8192x8192 layer (M=4096, N=8192, K=8192, with the
+    # classifier dot): 2.903 GB read + 0.265 GB written; its algorithmic
+    # operand + output bytes are 1.09 GB.  Other configs: not captured.
+    traffic = {"bytes_per_launch": 3.168e9, "launch": "configs[2] forward 4096x8192x8192 (+dot)",
+               "algorithmic_bytes": 1.087e9} if CFG.name == "c2" else None
     achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0
     step_flops = CFG.flops_per_sample() * B
     breakdown = {s["name"]: round(s["ms"] / max(1, s["launches"]), 4) for s in sites}
 
     result = None
     if rank == 0:
-        cpu = cpu_baseline(steps=1, batch=128) if (world == 1 and not args.no_cpu) else None
+        # configs[4]'s CPU step (1.4 B parameters, single-threaded GEMM) would
+        # take hours even at 128 rows: not timed.
+        cpu = cpu_baseline(steps=1, batch=128) if (world == 1 and not args.no_cpu and
+                                                   CFG.name != "c4") else None
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (uniform [0,1) inputs seed=rank, uniform labels, "
-                    "Kaiming-uniform weights seed 1)",
-            "config": {"workload": "BASELINE configs[2]: MLP 784-8192-8192-10, SGD momentum 0.9 "
-                                   "lr 0.01, per-rank batch 4096",
+            "data": f"synthetic ({'uniform [0,1)' if CFG.inputs == 'uniform' else 'N(0,1)'} "
+                    "inputs seed=rank, uniform labels, Kaiming-uniform weights seed 1)",
+            "config": {"workload": describe(CFG),
                        "global_batch": world * B, "per_rank_batch": B,
-                       "parallelism": f"dp{world}", "l2": "working set > L2 (no flush needed)",
+                       "parallelism": f"dp{world}",
+                       "l2": "working set > L2 (no flush needed)" if CFG.n_params * 16 > 126e6
+                       else "working set fits in the 126 MB L2 and is not flushed between steps "
+                            "(a reference measurement, not the configs[2] line)",
                        "bucket_mb": args.bucket_mb if world > 1 else None},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": int(x.nbytes + t.nbytes), "d2h_bytes_per_step": 4,
                     "ms_per_step": e2e_ms / args.steps},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak,
                          "unit": "TFLOP/s", "frac": achieved / tf32_peak if tf32_peak else None,
-                         "traffic": traffic["bytes_per_launch"], "traffic_detail": traffic,
+                         "traffic": traffic["bytes_per_launch"] if traffic else None,
+                         "traffic_detail": traffic,
                          "kernel": "tc_gemm_kernel (3xTF32 tcgen05, all GEMM launches of the step)",
                          "peak_note": f"{peak_src} bf16 dense {peaks['bf16_tflops']} TFLOP/s / 2 "
                                       "(tf32 rate) / 3 (products per FP32 product)",
@@ -311,7 +352,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--bucket-mb", type=int, default=64)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--config", default="c2", choices=["c2", "c0", "c1", "c4"],
+                    help="BASELINE config (default configs[2], the metric's)")
     args = ap.parse_args()
+    set_config(args.config)
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
