@@ -1083,13 +1083,19 @@ static int64_t chunk_kblocks() {
   return v;
 }
 
-// The pair kernel is correct but measured ~4% slower than the single-CTA
-// kernel on the MLP's products (4096 x 8192 x 8192: 2.32 vs 2.23 ms on B200),
-// so AUTO/TC take it only when ORCA_GEMM_PAIR=1.
-static bool pair_enabled() {
-  static const bool v = [] {
+// Which products take the pair kernel under AUTO/TC.  Measured in the
+// configs[2] step on B200 (power-capped, same box, A/B): for the dW products,
+// whose A operand (the activations, read transposed) is MN-major, the pair
+// kernel is 10 % faster (2.27 vs 2.53 ms for 8192 x 8192 x 4096) -- each CTA
+// stages half of the MN-major B tile, the costlier orientation to load; for
+// the K-major-A products it is 4-6 % slower.  ORCA_GEMM_PAIR=0 / =1 turns it
+// off / on for every product with M >= 256.
+static int pair_policy() {
+  static const int v = [] {
     const char* e = getenv("ORCA_GEMM_PAIR");
-    return e && e[0] == '1';
+    if (e && e[0] == '0') return 0;
+    if (e && e[0] == '1') return 1;
+    return 2;   // MN-major A only
   }();
   return v;
 }
@@ -1158,8 +1164,10 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
                                        SMEM_BYTES_DOT));
     attr_set[ctx->device] = true;
   }
+  const int policy = pair_policy();
   const bool pair = !range && (path == GEMM_TC_PAIR ||
-                               (path != GEMM_TC_SINGLE && pair_enabled() && M >= 2 * BM));
+                               (path != GEMM_TC_SINGLE && M >= 2 * BM &&
+                                (policy == 1 || (policy == 2 && A.mn_major))));
   // B tile rows per CTA: all BN columns, or the CTA's half of them in a pair.
   const int b_rows = pair ? PB_ROWS : BN;
   CUtensorMap ma, mb;

@@ -53,9 +53,10 @@ constexpr int HEAD_MAX_CLASSES = 16;
 
 // AUTO: tensor cores when eligible and large enough; SIMT: FFMA kernels only;
 // TC: tensor cores whenever eligible (skinny/unaligned shapes still use SIMT).
-// On the tensor cores, AUTO and TC take the single-CTA kernel (the CTA-pair
-// kernel when the environment sets ORCA_GEMM_PAIR=1 and M >= 256);
-// TC_SINGLE and TC_PAIR force one or the other.
+// On the tensor cores, AUTO and TC take the CTA-pair kernel for products with
+// an MN-major A operand and M >= 256 (the dW products), the single-CTA kernel
+// otherwise (ORCA_GEMM_PAIR=0 / =1: never / always); TC_SINGLE and TC_PAIR
+// force one or the other.
 enum GemmPath : int { GEMM_AUTO = 0, GEMM_SIMT = 1, GEMM_TC = 2, GEMM_TC_SINGLE = 3,
                       GEMM_TC_PAIR = 4 };
 inline bool gemm_path_is_tc(int path) {
