@@ -298,7 +298,7 @@ constexpr int SMEM_BYTES_DOT = SMEM_BYTES + 32 * 8 * DOT_SLOT * 4;
 constexpr int EPI_WARPS = 8;                         // 2 per TMEM lane quarter, 128 columns each
 constexpr int THREADS = 64 + 32 * EPI_WARPS;         // producer + MMA + epilogue warps
 constexpr int TMEM_COLS = 2 * BN;                    // two accumulator buffers
-constexpr int GROUP_M = 8;
+constexpr int GROUP_M = 8;                           // default raster group (ORCA_GEMM_GROUP_M)
 constexpr int DEFAULT_CHUNK_KB = 8;                  // k-blocks per accumulation chunk
 constexpr int SHORT_K_CHUNK_KB = 4;                  // ... when the whole K is <= 64 k-blocks
 
@@ -319,6 +319,7 @@ struct Params {
   int* dev_err;
   int* tile_ctr;           // zeroed before each launch of tc_gemm_kernel
   int64_t tile_begin, tile_end;   // tiles [tile_begin, tile_end) of the raster order
+  int group_m;             // tile rows per raster group (consecutive tiles share B columns)
 };
 
 // Dynamic tile scheduling of tc_gemm_kernel: the producer takes the next tile
@@ -362,7 +363,8 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int mn_major, in
 }
 
 __device__ __forceinline__ void tile_coords(int64_t tile, int64_t num_m, int64_t num_n,
-                                            int64_t& tm, int64_t& tn) {
+                                            int64_t& tm, int64_t& tn, int group_m) {
+  const int64_t GROUP_M = group_m;
   const int64_t group_size = (int64_t)GROUP_M * num_n;
   const int64_t group = tile / group_size;
   const int64_t first_m = group * GROUP_M;
@@ -581,7 +583,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         mbar_arrive(&tq_full[slot]);
         if (t >= p.tile_end) break;
         int64_t tm, tn;
-        tile_coords(t, num_m, num_n, tm, tn);
+        tile_coords(t, num_m, num_n, tm, tn, p.group_m);
         for (int64_t kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.dev_err, 20)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[stage], A_STAGE + B_STAGE);
@@ -688,7 +690,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       if (lane == 0) mbar_arrive(&tq_empty[slot]);
       if (tile < 0) break;
       int64_t tm, tn;
-      tile_coords(tile, num_m, num_n, tm, tn);
+      tile_coords(tile, num_m, num_n, tm, tn, p.group_m);
       float acc[128];   // 0 + x == x: the first chunk adds into zeros exactly
 #pragma unroll
       for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
@@ -847,7 +849,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
       bool ok = true;
       for (int64_t tile = cluster; tile < num_tiles && ok; tile += nclusters) {
         int64_t tm, tn;
-        tile_coords(tile, num_m, num_n, tm, tn);
+        tile_coords(tile, num_m, num_n, tm, tn, p.group_m);
         const int64_t a_row = tm * 2 * BM + (int64_t)rank * BM;
         const int64_t b_col = tn * BN + (int64_t)rank * PB_ROWS;
         for (int64_t kb = 0; kb < nk; ++kb) {
@@ -959,7 +961,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
     bool ok = true;
     for (int64_t tile = cluster; tile < num_tiles && ok; tile += nclusters) {
       int64_t tm, tn;
-      tile_coords(tile, num_m, num_n, tm, tn);
+      tile_coords(tile, num_m, num_n, tm, tn, p.group_m);
       float acc[128];
 #pragma unroll
       for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
@@ -1183,6 +1185,12 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
   p.ep = ep;
   p.dev_err = ctx->dev_err;
   p.tile_ctr = ctx->tile_ctr;
+  static const int group_m = [] {
+    const char* e = getenv("ORCA_GEMM_GROUP_M");
+    const long v = e ? strtol(e, nullptr, 10) : 0;
+    return (int)(v > 0 ? v : GROUP_M);
+  }();
+  p.group_m = group_m;
   // Measured on B200 (mean |error| / sum|a*b|, relu-activation x weight data):
   // 8 k-blocks per chunk gives 1.6e-8 at K = 8192 and 5e-8 at K = 784, 4 gives
   // 2.6e-8 at K = 784; a single chain gives 1.0e-6 at K = 8192.  Serial FP32
