@@ -318,6 +318,7 @@ struct Params {
   Epilogue ep;
   int* dev_err;
   int* tile_ctr;           // zeroed before each launch of tc_gemm_kernel
+  int a_load, b_load;      // LOAD_* mode of each operand's tensor map
   int64_t tile_begin, tile_end;   // tiles [tile_begin, tile_end) of the raster order
   int group_m;             // tile rows per raster group (consecutive tiles share B columns)
 };
@@ -374,9 +375,15 @@ __device__ __forceinline__ void tile_coords(int64_t tile, int64_t num_m, int64_t
   tn = r / gm;
 }
 
+// Operand load modes (Params::a_load / b_load): K-major (one 3-D box),
+// MN-major as one 3-D box per 32-wide chunk, or MN-major as one 4-D box.
+constexpr int LOAD_K = 0, LOAD_MN_CHUNKS = 1, LOAD_MN_4D = 2;
+
 __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
-                                             int mn_major, int rows, int64_t mn0, int64_t k0) {
-  if (mn_major) {
+                                             int mode, int rows, int64_t mn0, int64_t k0) {
+  if (mode == LOAD_MN_4D) {
+    tma_load_4d(dst, map, bar, 0, (int)k0, 0, (int)(mn0 / 32));
+  } else if (mode == LOAD_MN_CHUNKS) {
     for (int c = 0; c < rows / 32; ++c)
       tma_load_3d(dst + c * 4096, map, bar, (int)(mn0 + 32 * c), (int)k0, 0);
   } else {
@@ -426,9 +433,11 @@ __device__ __forceinline__ void dot_group(const Epilogue& ep, int64_t n_first, c
 
 // load_operand for the odd CTA of a pair: completion on the even CTA's barrier.
 __device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMap* map,
-                                                  uint32_t bar_cl, int mn_major, int rows,
+                                                  uint32_t bar_cl, int mode, int rows,
                                                   int64_t mn0, int64_t k0) {
-  if (mn_major) {
+  if (mode == LOAD_MN_4D) {
+    tma_load_4d_pair(dst, map, bar_cl, 0, (int)k0, 0, (int)(mn0 / 32));
+  } else if (mode == LOAD_MN_CHUNKS) {
     for (int c = 0; c < rows / 32; ++c)
       tma_load_3d_pair(dst + c * 4096, map, bar_cl, (int)(mn0 + 32 * c), (int)k0, 0);
   } else {
@@ -587,9 +596,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         for (int64_t kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.dev_err, 20)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[stage], A_STAGE + B_STAGE);
-          load_operand(a_tiles + stage * A_STAGE, &map_a, &full_bar[stage], p.a_mn, BM, tm * BM,
+          load_operand(a_tiles + stage * A_STAGE, &map_a, &full_bar[stage], p.a_load, BM, tm * BM,
                        kb * BK);
-          load_operand(b_tiles + stage * B_STAGE, &map_b, &full_bar[stage], p.b_mn, BN, tn * BN,
+          load_operand(b_tiles + stage * B_STAGE, &map_b, &full_bar[stage], p.b_load, BN, tn * BN,
                        kb * BK);
           issued[stage] = (int)phase;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -859,16 +868,16 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
           }
           if (even) {
             mbar_arrive_expect_tx(&full_bar[stage], 2 * (PA_STAGE + PB_STAGE));
-            load_operand(a_tiles + stage * PA_STAGE, &map_a, &full_bar[stage], p.a_mn, BM, a_row,
+            load_operand(a_tiles + stage * PA_STAGE, &map_a, &full_bar[stage], p.a_load, BM, a_row,
                          kb * BK);
-            load_operand(b_tiles + stage * PB_STAGE, &map_b, &full_bar[stage], p.b_mn, PB_ROWS,
+            load_operand(b_tiles + stage * PB_STAGE, &map_b, &full_bar[stage], p.b_load, PB_ROWS,
                          b_col, kb * BK);
             issued[stage] = (int)phase;
           } else {
             const uint32_t bar_e = cluster_addr(&full_bar[stage], 0);
-            load_operand_pair(a_tiles + stage * PA_STAGE, &map_a, bar_e, p.a_mn, BM, a_row,
+            load_operand_pair(a_tiles + stage * PA_STAGE, &map_a, bar_e, p.a_load, BM, a_row,
                               kb * BK);
-            load_operand_pair(b_tiles + stage * PB_STAGE, &map_b, bar_e, p.b_mn, PB_ROWS, b_col,
+            load_operand_pair(b_tiles + stage * PB_STAGE, &map_b, bar_e, p.b_load, PB_ROWS, b_col,
                               kb * BK);
             last_issue = global_ns();
           }
@@ -1052,6 +1061,34 @@ static orca_status make_map(CUtensorMap* map, const Operand& op, int64_t inner_e
   return ORCA_OK;
 }
 
+// An MN-major operand tile as ONE 4-D box {32 mn, BK k, 2 planes, rows/32
+// chunks}: dims {32, k_extent, 2, mn_extent/32} with the chunk index strided by
+// 128 B, so the box lands in shared memory exactly as rows/32 separate 3-D
+// boxes would (chunk c at 4 KB * c, plane at +2 KB, k rows 128 B apart, the
+// same 128-byte swizzle).  Only when mn_extent % 32 == 0, so every address the
+// box can touch lies inside the operand (past-the-end k rows are the only
+// out-of-bounds coordinates, and those are zero-filled).
+static bool make_map4d(CUtensorMap* map, const Operand& op, int64_t mn_extent, int64_t k_extent,
+                       int rows) {
+  static const bool enabled = [] {
+    const char* e = getenv("ORCA_TMA_4D");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled || mn_extent % 32 != 0 || rows % 32 != 0) return false;
+  auto encode = get_encode_fn();
+  if (!encode) return false;
+  const int64_t plane_stride = (int64_t)(op.lo - op.hi);
+  cuuint64_t dims[4] = {32, (cuuint64_t)k_extent, 2, (cuuint64_t)(mn_extent / 32)};
+  cuuint64_t strides[3] = {(cuuint64_t)(op.ld * 4), (cuuint64_t)(plane_stride * 4), 128};
+  cuuint32_t box[4] = {32, (cuuint32_t)BK, 2, (cuuint32_t)(rows / 32)};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(op.hi), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;   // otherwise the caller uses one 3-D box per chunk
+}
+
 static bool operand_ok(const Operand& op) {
   if (!op.hi || !op.lo) return false;
   if (op.lo <= op.hi) return false;
@@ -1173,15 +1210,32 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
   // B tile rows per CTA: all BN columns, or the CTA's half of them in a pair.
   const int b_rows = pair ? PB_ROWS : BN;
   CUtensorMap ma, mb;
+  int a_load = LOAD_K, b_load = LOAD_K;
   // A: K-major rows = M (extent {K, M}); MN-major rows = K (extent {M, K}).
-  if (A.mn_major) ORCA_TRY(make_map(&ma, A, M, K, 32, BK, true));
-  else ORCA_TRY(make_map(&ma, A, K, M, BK, BM, false));
-  if (B.mn_major) ORCA_TRY(make_map(&mb, B, N, K, 32, BK, true));
-  else ORCA_TRY(make_map(&mb, B, K, N, BK, b_rows, false));
+  if (A.mn_major) {
+    a_load = LOAD_MN_4D;
+    if (!make_map4d(&ma, A, M, K, BM)) {
+      a_load = LOAD_MN_CHUNKS;
+      ORCA_TRY(make_map(&ma, A, M, K, 32, BK, true));
+    }
+  } else {
+    ORCA_TRY(make_map(&ma, A, K, M, BK, BM, false));
+  }
+  if (B.mn_major) {
+    b_load = LOAD_MN_4D;
+    if (!make_map4d(&mb, B, N, K, b_rows)) {
+      b_load = LOAD_MN_CHUNKS;
+      ORCA_TRY(make_map(&mb, B, N, K, 32, BK, true));
+    }
+  } else {
+    ORCA_TRY(make_map(&mb, B, K, N, BK, b_rows, false));
+  }
   Params p;
   p.M = M; p.N = N; p.K = K;
   p.a_mn = A.mn_major ? 1 : 0;
   p.b_mn = B.mn_major ? 1 : 0;
+  p.a_load = a_load;
+  p.b_load = b_load;
   p.ep = ep;
   p.dev_err = ctx->dev_err;
   p.tile_ctr = ctx->tile_ctr;
