@@ -1290,7 +1290,8 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
 // (the next-layer dot) and are only reduced over column slices; dW and dX
 // share one pass over the activation.
 namespace head {
-constexpr int THREADS = 256;
+constexpr int THREADS = 128;          // 3 blocks / SM at ~140 registers: 8 rows of loads in flight
+constexpr int UNROLL = 8;             // rows per iteration (their loads are issued together)
 constexpr int ROW_CHUNK = 128;        // rows of g staged in shared memory at a time
 constexpr int MAX_ROW_BLOCKS = 64;
 
@@ -1345,11 +1346,11 @@ bwd_kernel(int64_t B, int64_t H, int C, int64_t rows, const float* __restrict__ 
     }
     __syncthreads();
     if (!active) continue;
-    for (int r = 0; r < nr; r += 4) {
-      const int cnt = std::min(4, nr - r);
-      float a[4][COLS];
+    for (int r = 0; r < nr; r += UNROLL) {
+      const int cnt = nr - r < UNROLL ? nr - r : UNROLL;
+      float a[UNROLL][COLS];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < UNROLL; ++u) {
         const int64_t idx = (c0 + r + u) * H + n0;
         if (u < cnt) {
           if (COLS == 2) {
@@ -1366,7 +1367,7 @@ bwd_kernel(int64_t B, int64_t H, int C, int64_t rows, const float* __restrict__ 
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < UNROLL; ++u) {
         if (u >= cnt) break;
         float gr[CP];
 #pragma unroll
