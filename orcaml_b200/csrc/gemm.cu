@@ -1,14 +1,20 @@
 // gemm.cu -- GEMM kernels of the MLP step (see gemm.cuh for the operand format).
 //
 //  * tc_gemm_kernel: persistent warp-specialised tcgen05 kernel.  One CTA per
-//    SM; warp 0 issues TMA tile loads (hi and lo planes in one 3-D box), warp 1
-//    issues tcgen05.mma kind::tf32 (three products per k-step into one TMEM
-//    accumulator), warps 2-5 drain the double-buffered TMEM accumulator through
-//    the fused epilogue.  128x256 tiles, BK = 16, 4-stage smem ring.
+//    SM taking tiles from a global counter; warp 0 issues TMA tile loads (hi
+//    and lo planes in one box), warp 1 issues tcgen05.mma kind::tf32 (three
+//    products per k-step into one TMEM accumulator), warps 2-9 drain the
+//    double-buffered TMEM accumulator through the fused epilogue (optionally
+//    forming the classifier layer's product on the way).  128x256 tiles,
+//    BK = 16, 4-stage smem ring.
+//  * tc_gemm_pair_kernel: the same on 256x256 tiles computed by a cluster of
+//    two CTAs with tcgen05.mma.cta_group::2 (used for the dW products).
 //  * simt_gemm_kernel: FFMA tiled kernel for shapes the tensor-core path does
 //    not take (tiny M/N, unaligned leading dimensions).
-//  * skinny kernels for the N <= 16 (logit layer, its dW) and K <= 16 (its dX)
-//    GEMMs of the classifier layer, which are memory-bound.
+//  * skinny kernels for N <= 16 and K <= 16 products (the classifier layer of
+//    models the fused head does not cover), which are memory-bound.
+//  * head kernels: the classifier layer (C <= 16) around the tensor-core
+//    kernels -- the slice reduction of its logits and its backward pass.
 //
 // The reference computes every product with `matrixmultiply::sgemm` in FP32
 // (orca-backend-cpu/src/backend.rs:130-221); all paths here are FP32-accurate:

@@ -4,15 +4,22 @@
 // backward, all_reduce_gradients, optimizer.step) for
 // Sequential(Linear, ReLU, ..., Linear) + CrossEntropyLoss + SGD/AdamW:
 //
-//   forward   Z = X @ W (+ b, ReLU) ........ tcgen05 GEMM, bias+ReLU+split epilogue
+//   forward   Z = X @ W (+ b, ReLU) ........ tcgen05 GEMM, bias+ReLU+split epilogue;
+//             the classifier layer (C <= 16) inside the last hidden GEMM's
+//             epilogue, reduced over column slices by head_logits
 //   loss      softmax-CE fwd+bwd ........... ce_kernel (one thread per row)
-//   backward  db = colsum(dZ) .............. colsum kernels
-//             dW = X^T @ dZ ................ GEMM, MN-major A and B (no transposes)
+//   backward  classifier dW, dX (masked) and the bias gradient of the layer
+//             below ........................ head_backward, one pass
+//             dW = X^T @ dZ ................ GEMM (CTA-pair kernel), MN-major A and
+//                                            B (no transposes); for layer 0 the
+//                                            input's column of ones adds db0
 //             dX = dZ @ W^T, * (X > 0) ..... GEMM, K-major B, ReLU-mask+split epilogue
+//             db of the classifier ......... colsum kernels
 //   exchange  all-reduce average of each layer's (dW, db) on the comm stream,
 //             started as soon as that layer's gradients exist
 //   update    SGD / SGD-momentum / AdamW kernels with the reference's per-op
-//             f32 rounding, writing the weights back as (hi, lo) planes.
+//             f32 rounding, writing the weights back as (hi, lo) planes; with a
+//             communicator each layer waits only for its own all-reduce.
 //
 // GEMM operands live as (hi, lo) plane pairs (gemm.cuh); the reference's
 // [in, out] weight layout (python/orca/nn/linear.py:29) is kept.
@@ -33,9 +40,8 @@ namespace orca {
 // ---------------------------------------------------------------- kernels
 // Softmax cross-entropy forward + backward for one row per thread, restating
 // python/orca/nn/loss.py:83-100 and the reverse sweep of the tape nodes it
-// records (orca-autograd/src/backend.rs; see oracle/orca_oracle.c
-// oc_softmax_ce for the node-by-node derivation).  row_loss[b] gets
-// sum_c -(t*ls); the mean is taken by ce_loss_kernel.
+// records (orca-autograd/src/backend.rs:1380-1793, node by node).  row_loss[b]
+// gets sum_c -(t*ls); the mean is taken by ce_loss_kernel.
 __global__ void ce_kernel(const float* __restrict__ P, const float* __restrict__ T, int64_t B,
                           int64_t C, float inv_b, float* __restrict__ dP,
                           float* __restrict__ row_loss) {
