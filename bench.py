@@ -234,9 +234,19 @@ def run_ours(args):
         return float(tt.item())
 
     # ---- device-resident step (value) ----
+    use_graph = args.graph and world == 1 and CFG.optimizer == "sgd"
+    if use_graph:
+        tr.graph_capture(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+
+    def device_step():
+        if use_graph:
+            tr.graph_step()
+        else:
+            tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+
     clocks = ClockSampler(local).__enter__()   # sampling from warm-up on
     for _ in range(args.warmup):
-        tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+        device_step()
     barrier()
     launches0 = be.launch_count()
     ev0 = torch.cuda.Event(enable_timing=True)
@@ -245,14 +255,24 @@ def run_ours(args):
     if True:
         barrier()
         ev0.record(stream)
-        tr.profile_begin()
+        if not use_graph:
+            tr.profile_begin()
         for _ in range(args.steps):
-            tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+            device_step()
         ev1.record(stream)
-        sites = tr.profile_end()
+        if not use_graph:
+            sites = tr.profile_end()
         barrier()
         clocks.__exit__(None, None, None)
     launches = be.launch_count() - launches0
+    if use_graph:
+        # The per-kernel breakdown comes from a few ordinary profiled steps
+        # (the replay is one launch, it cannot be split into sites).
+        tr.graph_release()
+        tr.profile_begin()
+        for _ in range(3):
+            tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+        sites = tr.profile_end()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_step = ms / args.steps
     value = world * B * args.steps / (ms / 1000.0)
@@ -307,7 +327,8 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": f"synthetic ({'uniform [0,1)' if CFG.inputs == 'uniform' else 'N(0,1)'} "
                     "inputs seed=rank, uniform labels, Kaiming-uniform weights seed 1)",
-            "config": {"workload": describe(CFG),
+            "config": {"workload": describe(CFG) + (" (device step as a CUDA graph)"
+                                                     if use_graph else ""),
                        "global_batch": world * B, "per_rank_batch": B,
                        "parallelism": f"dp{world}",
                        "l2": "working set > L2 (no flush needed)" if CFG.n_params * 16 > 126e6
@@ -352,6 +373,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--bucket-mb", type=int, default=64)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--graph", action="store_true",
+                    help="time the device-resident step as a captured CUDA graph (SGD, N=1)")
     ap.add_argument("--config", default="c2", choices=["c2", "c0", "c1", "c4"],
                     help="BASELINE config (default configs[2], the metric's)")
     args = ap.parse_args()

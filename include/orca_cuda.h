@@ -313,6 +313,17 @@ orca_status orca_mlp_forward(orca_mlp* mlp, const float* x, const float* t, floa
                              float* loss);
 /* Number of this library's kernels the last step launched. */
 orca_status orca_mlp_launches_per_step(const orca_mlp* mlp, int* count);
+/* CUDA-graph form of orca_mlp_step_device for fixed device buffers: _capture
+ * records one step (it runs one ordinary step first if the optimizer has not
+ * stepped yet), _replay launches the recorded step -- one launch for the
+ * whole step, for models whose steps are launch-bound.  SGD only (AdamW's
+ * bias corrections change every step: ORCA_NOT_IMPLEMENTED), no communicator,
+ * not while profiling.  Parameters and optimizer state live in the trainer,
+ * so replays continue training exactly as ordinary steps would. */
+orca_status orca_mlp_graph_capture(orca_mlp* mlp, const float* x_dev, const float* t_dev,
+                                   float* loss_dev);
+orca_status orca_mlp_graph_replay(orca_mlp* mlp);
+orca_status orca_mlp_graph_release(orca_mlp* mlp);
 /* Per-kernel-group timing of later steps: CUDA events recorded on the compute
  * stream around each GEMM / CE / column-sum / optimizer group.  _end
  * synchronises and aggregates; _site reads one group (name, total ms over

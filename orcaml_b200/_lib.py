@@ -101,6 +101,9 @@ _SIGS = {
                      PP], c_int),
     "orca_scatter": ([c_void_p, c_void_p, c_int64, c_void_p, c_void_p, P_int64, c_int, P_int64,
                       c_int, c_int, PP], c_int),
+    "orca_mlp_graph_capture": ([c_void_p, c_void_p, c_void_p, c_void_p], c_int),
+    "orca_mlp_graph_replay": ([c_void_p], c_int),
+    "orca_mlp_graph_release": ([c_void_p], c_int),
     "orca_mlp_state_numel": ([c_void_p, c_int, c_int, P_int64], c_int),
     "orca_mlp_get_state": ([c_void_p, c_int, c_int, c_void_p, c_int64], c_int),
     "orca_mlp_set_state": ([c_void_p, c_int, c_int, c_void_p, c_int64], c_int),

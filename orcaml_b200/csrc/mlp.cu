@@ -302,6 +302,9 @@ struct orca_mlp {
   cudaEvent_t ev_layer[64];         // layer's gradients ready (compute stream)
   cudaEvent_t ev_reduced[64];       // layer's gradients averaged (comm stream)
   int last_launches = 0;
+  // Captured step (orca_mlp_graph_*).
+  cudaGraphExec_t graph_exec = nullptr;
+  int graph_launches = 0;
   // Optional per-kernel-group timing: CUDA events recorded on the compute
   // stream around each group of a step while profiling is on.
   struct ProfSite { std::string name; double flops = 0, bytes = 0; double ms = 0; int count = 0;
@@ -537,6 +540,7 @@ orca_status orca_mlp_destroy(orca_mlp* m) {
   cudaSetDevice(m->ctx->device);
   sync_stream_for(m->ctx, m->ctx->stream, m->ctx->sync_timeout_s);
   sync_stream_for(m->ctx, m->ctx->comm_stream, m->ctx->sync_timeout_s);
+  if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
   for (void* p : m->allocs) cudaFree(p);
   if (m->host_stage) cudaFreeHost(m->host_stage);
   for (int l = 0; l < 64; ++l)
@@ -705,6 +709,71 @@ orca_status orca_mlp_step_device(orca_mlp* m, const float* x_dev, const float* t
   ORCA_TRY(check_ctx(m->ctx));
   std::lock_guard<std::mutex> lk(m->ctx->mu);
   return step_device_locked(m, x_dev, t_dev, loss_dev);
+}
+
+orca_status orca_mlp_graph_capture(orca_mlp* m, const float* x_dev, const float* t_dev,
+                                   float* loss_dev) {
+  if (!m || !x_dev || !t_dev) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (m->opt != ORCA_OPT_SGD)
+    return fail(ORCA_NOT_IMPLEMENTED, "graph capture: SGD only (AdamW's per-step constants)");
+  if (m->comm) return fail(ORCA_INVALID_ARGUMENT, "graph capture: detach the communicator");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  if (m->profiling) return fail(ORCA_INVALID_ARGUMENT, "graph capture: profiling is on");
+  orca_ctx* ctx = m->ctx;
+  if (m->graph_exec) {
+    cudaGraphExecDestroy(m->graph_exec);
+    m->graph_exec = nullptr;
+  }
+  // The first momentum step differs (v = g); capture a steady-state step.  The
+  // ordinary step also performs every one-time set-up (kernel attributes,
+  // cluster occupancy) outside the capture.
+  if (!m->vel_init) ORCA_TRY(step_device_locked(m, x_dev, t_dev, loss_dev));
+  ORCA_TRY(sync_stream(ctx));
+  const uint64_t l0 = ctx->launches.load();
+  ORCA_CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  const orca_status s = step_device_locked(m, x_dev, t_dev, loss_dev);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+  const int launches = (int)(ctx->launches.load() - l0);
+  ctx->launches -= (uint64_t)launches;      // captured, not run
+  if (s != ORCA_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return s;
+  }
+  if (e != cudaSuccess || !graph)
+    return fail(ORCA_CUDA_ERROR, "graph capture failed: %s", cudaGetErrorString(e));
+  const cudaError_t ei = cudaGraphInstantiate(&m->graph_exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ei != cudaSuccess) {
+    m->graph_exec = nullptr;
+    return fail(ORCA_CUDA_ERROR, "graph instantiation failed: %s", cudaGetErrorString(ei));
+  }
+  m->graph_launches = launches;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_graph_replay(orca_mlp* m) {
+  if (!m) return fail(ORCA_INVALID_ARGUMENT, "null mlp");
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  if (!m->graph_exec) return fail(ORCA_INVALID_ARGUMENT, "no captured step");
+  if (m->comm) return fail(ORCA_INVALID_ARGUMENT, "graph replay: a communicator is attached");
+  ORCA_CUDA_TRY(cudaGraphLaunch(m->graph_exec, m->ctx->stream));
+  count_launch(m->ctx, (uint64_t)m->graph_launches);
+  m->last_launches = m->graph_launches;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_graph_release(orca_mlp* m) {
+  if (!m) return ORCA_OK;
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  if (m->graph_exec) {
+    ORCA_TRY(sync_stream(m->ctx));
+    cudaGraphExecDestroy(m->graph_exec);
+    m->graph_exec = nullptr;
+  }
+  return ORCA_OK;
 }
 
 orca_status orca_mlp_step(orca_mlp* m, const float* x, const float* t, float* loss) {

@@ -250,6 +250,19 @@ class MlpTrainer:
         L.check(L.load().orca_mlp_step_device(self._h, ctypes.c_void_p(x_dev), ctypes.c_void_p(t_dev),
                                               ctypes.c_void_p(loss_dev) if loss_dev else None))
 
+    def graph_capture(self, x_dev: int, t_dev: int, loss_dev: int = 0):
+        """Record one step on fixed device buffers as a CUDA graph (SGD, no
+        communicator); graph_step() then replays it with one launch."""
+        L.check(L.load().orca_mlp_graph_capture(self._h, ctypes.c_void_p(x_dev),
+                                                ctypes.c_void_p(t_dev),
+                                                ctypes.c_void_p(loss_dev) if loss_dev else None))
+
+    def graph_step(self):
+        L.check(L.load().orca_mlp_graph_replay(self._h))
+
+    def graph_release(self):
+        L.check(L.load().orca_mlp_graph_release(self._h))
+
     def forward(self, x, t=None):
         """Logits [batch, classes] (and the loss when t is given)."""
         x, t = self._check_batch(x, t)
