@@ -278,20 +278,35 @@ def run_ours(args):
     value = world * B * args.steps / (ms / 1000.0)
     loss_val = float(be.to_f32_vec(loss_s)[0])
 
-    # ---- end to end through the host API: pinned inputs, H2D + D2H inside ----
-    xp = torch.empty(x.shape, dtype=torch.float32, pin_memory=True)
-    tp = torch.empty(t.shape, dtype=torch.float32, pin_memory=True)
-    xp.numpy()[:] = x
-    tp.numpy()[:] = t
+    # ---- end to end through the host API: page-locked inputs, H2D + D2H inside ----
+    # "staged" (default): the input pipeline -- batch k+1 is copied on the
+    # step runner's copy stream while step k computes (two page-locked
+    # buffers, two device slots); "step": orca_mlp_step copies, then computes.
+    # Either way every step copies its inputs and reads its loss back.
+    from orcaml_b200.dataloader import pinned_empty
+    bufs = []
+    for _ in range(2):
+        xp, tp = pinned_empty(x.shape), pinned_empty(t.shape)
+        xp[:], tp[:] = x, t
+        bufs.append((xp, tp))
     host_loss = ctypes.c_float()
-    for _ in range(max(1, args.warmup // 2)):
-        tr.step_host_ptr(xp.data_ptr(), tp.data_ptr(), host_loss)
+
+    def e2e_steps(n):
+        if args.e2e == "step":
+            for _ in range(n):
+                tr.step_host_ptr(bufs[0][0].ctypes.data, bufs[0][1].ctypes.data, host_loss)
+            return
+        tr.stage_batch(0, *bufs[0])
+        for k in range(n):
+            if k + 1 < n:
+                tr.stage_batch((k + 1) % 2, *bufs[(k + 1) % 2])
+            tr.step_staged(k % 2)                  # reads the loss back
+    e2e_steps(max(1, args.warmup // 2))
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        tr.step_host_ptr(xp.data_ptr(), tp.data_ptr(), host_loss)   # reads the loss back
+    e2e_steps(args.steps)
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
@@ -337,7 +352,9 @@ def run_ours(args):
                        "bucket_mb": args.bucket_mb if world > 1 else None},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": int(x.nbytes + t.nbytes), "d2h_bytes_per_step": 4,
-                    "ms_per_step": e2e_ms / args.steps},
+                    "ms_per_step": e2e_ms / args.steps,
+                    "pipeline": "copy of batch k+1 overlapped with step k (orca_mlp_stage_batch)"
+                    if args.e2e == "staged" else "copy then step (orca_mlp_step)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak,
                          "unit": "TFLOP/s", "frac": achieved / tf32_peak if tf32_peak else None,
                          "traffic": traffic["bytes_per_launch"] if traffic else None,
@@ -373,6 +390,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--bucket-mb", type=int, default=64)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--e2e", default="staged", choices=["staged", "step"],
+                    help="end-to-end leg: copies overlapped with the previous step, or not")
     ap.add_argument("--graph", action="store_true",
                     help="time the device-resident step as a captured CUDA graph (SGD, N=1)")
     ap.add_argument("--config", default="c2", choices=["c2", "c0", "c1", "c4"],

@@ -308,6 +308,25 @@ orca_status orca_mlp_step(orca_mlp* mlp, const float* x, const float* t, float* 
  * loss_dev (device, nullable) receives the loss; nothing is synchronised. */
 orca_status orca_mlp_step_device(orca_mlp* mlp, const float* x_dev, const float* t_dev,
                                  float* loss_dev);
+/* Input pipeline (the device side of DataLoader._collate,
+ * python/orca/data/dataloader.py:309-350): a batch is staged into one of
+ * ORCA_MLP_STAGE_SLOTS device slots by a host->device copy on the trainer's
+ * own copy stream, so the copy of batch k+1 runs while step k computes.
+ * _stage_batch returns at once when x and t are page-locked (cudaHostAlloc /
+ * orca_host_alloc / cudaHostRegister); the host memory must then stay
+ * unchanged until the step that consumes the slot has returned with its loss.
+ * Pageable sources are copied after a bounded host wait for the slot (the
+ * call returns once the data has left the host buffer).  Device pointers are
+ * refused.  _step_staged runs orca_mlp_step on the slot's batch, ordered
+ * after its copy; *loss (nullable) is read back as orca_mlp_step does.  A slot
+ * is consumed by one step; stepping on a slot with nothing staged is
+ * ORCA_INVALID_ARGUMENT. */
+#define ORCA_MLP_STAGE_SLOTS 2
+orca_status orca_mlp_stage_batch(orca_mlp* mlp, int slot, const float* x, const float* t);
+orca_status orca_mlp_step_staged(orca_mlp* mlp, int slot, float* loss);
+/* Page-locked host memory for staged batches (cudaHostAlloc, portable). */
+orca_status orca_host_alloc(size_t bytes, void** out);
+orca_status orca_host_free(void* ptr);
 /* Forward + loss only (no update): logits_host [batch, classes] and *loss. */
 orca_status orca_mlp_forward(orca_mlp* mlp, const float* x, const float* t, float* logits,
                              float* loss);

@@ -104,6 +104,10 @@ _SIGS = {
     "orca_mlp_graph_capture": ([c_void_p, c_void_p, c_void_p, c_void_p], c_int),
     "orca_mlp_graph_replay": ([c_void_p], c_int),
     "orca_mlp_graph_release": ([c_void_p], c_int),
+    "orca_mlp_stage_batch": ([c_void_p, c_int, c_void_p, c_void_p], c_int),
+    "orca_mlp_step_staged": ([c_void_p, c_int, c_void_p], c_int),
+    "orca_host_alloc": ([c_size_t, PP], c_int),
+    "orca_host_free": ([c_void_p], c_int),
     "orca_mlp_state_numel": ([c_void_p, c_int, c_int, P_int64], c_int),
     "orca_mlp_get_state": ([c_void_p, c_int, c_int, c_void_p, c_int64], c_int),
     "orca_mlp_set_state": ([c_void_p, c_int, c_int, c_void_p, c_int64], c_int),

@@ -84,6 +84,9 @@ void ctx_release(orca_ctx* ctx);
 // context's deadline.
 orca_status sync_stream(orca_ctx* ctx);
 orca_status sync_stream_for(orca_ctx* ctx, cudaStream_t stream, double timeout_s);
+// Host wait for an event, polled up to timeout_s (ORCA_TIMEOUT after it).  An
+// event never recorded counts as complete.
+orca_status wait_event_for(cudaEvent_t event, double timeout_s);
 // Device -> (pageable) host copy after the compute stream.  A copy into
 // pageable memory blocks the calling thread until the stream reaches it, with
 // no bound, so the stream is first drained with the deadline: a stream that

@@ -302,6 +302,15 @@ struct orca_mlp {
   cudaEvent_t ev_layer[64];         // layer's gradients ready (compute stream)
   cudaEvent_t ev_reduced[64];       // layer's gradients averaged (comm stream)
   int last_launches = 0;
+  // Input staging (orca_mlp_stage_batch / _step_staged): batches copied
+  // host->device on the trainer's own stream into one of the slots while the
+  // previous step computes; allocated on first use.
+  cudaStream_t copy_stream = nullptr;
+  float* slot_x[ORCA_MLP_STAGE_SLOTS] = {};
+  float* slot_t[ORCA_MLP_STAGE_SLOTS] = {};
+  cudaEvent_t ev_staged[ORCA_MLP_STAGE_SLOTS] = {};     // slot's copy done (copy stream)
+  cudaEvent_t ev_consumed[ORCA_MLP_STAGE_SLOTS] = {};   // slot read by its step (compute stream)
+  bool slot_ready[ORCA_MLP_STAGE_SLOTS] = {};
   // Captured step (orca_mlp_graph_*).
   cudaGraphExec_t graph_exec = nullptr;
   int graph_launches = 0;
@@ -540,6 +549,14 @@ orca_status orca_mlp_destroy(orca_mlp* m) {
   cudaSetDevice(m->ctx->device);
   sync_stream_for(m->ctx, m->ctx->stream, m->ctx->sync_timeout_s);
   sync_stream_for(m->ctx, m->ctx->comm_stream, m->ctx->sync_timeout_s);
+  if (m->copy_stream) {
+    sync_stream_for(m->ctx, m->copy_stream, m->ctx->sync_timeout_s);
+    cudaStreamDestroy(m->copy_stream);
+  }
+  for (int i = 0; i < ORCA_MLP_STAGE_SLOTS; ++i) {
+    if (m->ev_staged[i]) cudaEventDestroy(m->ev_staged[i]);
+    if (m->ev_consumed[i]) cudaEventDestroy(m->ev_consumed[i]);
+  }
   if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
   for (void* p : m->allocs) cudaFree(p);
   if (m->host_stage) cudaFreeHost(m->host_stage);
@@ -683,8 +700,11 @@ orca_status orca_mlp_attach_comm(orca_mlp* m, orca_comm* comm, size_t bucket_byt
   return ORCA_OK;
 }
 
+// One step on device inputs.  inputs_read (nullable) is recorded on the
+// compute stream once x_dev and t_dev have been read (the input split and the
+// target copy come first), after which their buffers may be overwritten.
 static orca_status step_device_locked(orca_mlp* m, const float* x_dev, const float* t_dev,
-                                      float* loss_dev) {
+                                      float* loss_dev, cudaEvent_t inputs_read = nullptr) {
   orca_ctx* ctx = m->ctx;
   const uint64_t l0 = ctx->launches.load();
   const int64_t B = m->B, C = m->dims[m->L];
@@ -694,6 +714,7 @@ static orca_status step_device_locked(orca_mlp* m, const float* x_dev, const flo
   if (t_dev != m->t_buf)
     ORCA_CUDA_TRY(cudaMemcpyAsync(m->t_buf, t_dev, (size_t)(B * C) * 4, cudaMemcpyDeviceToDevice,
                                   ctx->stream));
+  if (inputs_read) ORCA_CUDA_TRY(cudaEventRecord(inputs_read, ctx->stream));
   ORCA_TRY(mlp_forward_impl(m, true));
   ORCA_TRY(mlp_backward_impl(m));
   ORCA_TRY(mlp_update_impl(m));
@@ -776,6 +797,22 @@ orca_status orca_mlp_graph_release(orca_mlp* m) {
   return ORCA_OK;
 }
 
+// Loss and the device error word come back through pinned memory (the copies
+// do not block), then one bounded wait covers the whole step.
+static orca_status read_loss_locked(orca_mlp* m, float* loss) {
+  orca_ctx* ctx = m->ctx;
+  ORCA_CUDA_TRY(cudaMemcpyAsync(&m->host_stage[0], m->loss, 4, cudaMemcpyDeviceToHost,
+                                ctx->stream));
+  ORCA_CUDA_TRY(cudaMemcpyAsync(&m->host_stage[1], ctx->dev_err, 4, cudaMemcpyDeviceToHost,
+                                ctx->stream));
+  ORCA_TRY(finish_sync(m));
+  *loss = m->host_stage[0];
+  int h;
+  memcpy(&h, &m->host_stage[1], sizeof(int));
+  if (h != DEV_OK) return check_device_error(ctx);   // clears the word, maps the code
+  return ORCA_OK;
+}
+
 orca_status orca_mlp_step(orca_mlp* m, const float* x, const float* t, float* loss) {
   if (!m || !x || !t) return fail(ORCA_INVALID_ARGUMENT, "null argument");
   ORCA_TRY(check_ctx(m->ctx));
@@ -787,19 +824,87 @@ orca_status orca_mlp_step(orca_mlp* m, const float* x, const float* t, float* lo
   ORCA_CUDA_TRY(cudaMemcpyAsync(m->t_buf, t, (size_t)(B * C) * 4, cudaMemcpyHostToDevice,
                                 ctx->stream));
   ORCA_TRY(step_device_locked(m, m->x_stage, m->t_buf, nullptr));
-  if (loss) {
-    // Loss and the device error word come back through pinned memory (the
-    // copies do not block), then one bounded wait covers the whole step.
-    ORCA_CUDA_TRY(cudaMemcpyAsync(&m->host_stage[0], m->loss, 4, cudaMemcpyDeviceToHost,
-                                  ctx->stream));
-    ORCA_CUDA_TRY(cudaMemcpyAsync(&m->host_stage[1], ctx->dev_err, 4, cudaMemcpyDeviceToHost,
-                                  ctx->stream));
-    ORCA_TRY(finish_sync(m));
-    *loss = m->host_stage[0];
-    int h;
-    memcpy(&h, &m->host_stage[1], sizeof(int));
-    if (h != DEV_OK) return check_device_error(ctx);   // clears the word, maps the code
+  if (loss) return read_loss_locked(m, loss);
+  return ORCA_OK;
+}
+
+// Memory type of a host pointer: 1 page-locked, 0 pageable, -1 device or
+// managed memory (refused).
+static int host_memory_kind(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
   }
+  if (a.type == cudaMemoryTypeHost) return 1;
+  if (a.type == cudaMemoryTypeUnregistered) return 0;
+  return -1;
+}
+
+static orca_status ensure_staging(orca_mlp* m) {
+  if (m->copy_stream) return ORCA_OK;
+  const size_t xb = (size_t)(m->B * m->dims[0]) * 4, tb = (size_t)(m->B * m->dims[m->L]) * 4;
+  for (int i = 0; i < ORCA_MLP_STAGE_SLOTS; ++i) {
+    if (!m->ev_staged[i])
+      ORCA_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_staged[i], cudaEventDisableTiming));
+    if (!m->ev_consumed[i])
+      ORCA_CUDA_TRY(cudaEventCreateWithFlags(&m->ev_consumed[i], cudaEventDisableTiming));
+    if (m->slot_x[i]) continue;
+    void* p = nullptr;
+    if (cudaMalloc(&p, xb + tb) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(ORCA_CUDA_ERROR, "staging slot allocation (%zu bytes) failed", xb + tb);
+    }
+    m->allocs.push_back(p);
+    m->slot_x[i] = static_cast<float*>(p);
+    m->slot_t[i] = reinterpret_cast<float*>(static_cast<char*>(p) + xb);
+  }
+  ORCA_CUDA_TRY(cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking));
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_stage_batch(orca_mlp* m, int slot, const float* x, const float* t) {
+  if (!m || !x || !t) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (slot < 0 || slot >= ORCA_MLP_STAGE_SLOTS)
+    return fail(ORCA_INVALID_ARGUMENT, "slot must be in [0, %d)", ORCA_MLP_STAGE_SLOTS);
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  orca_ctx* ctx = m->ctx;
+  const int kx = host_memory_kind(x), kt = host_memory_kind(t);
+  if (kx < 0 || kt < 0)
+    return fail(ORCA_INVALID_ARGUMENT, "stage_batch takes host memory (use orca_mlp_step_device)");
+  ORCA_TRY(ensure_staging(m));
+  if (kx == 1 && kt == 1) {
+    // Fully asynchronous: the copy waits on the device until the slot's last
+    // step has read it.
+    ORCA_CUDA_TRY(cudaStreamWaitEvent(m->copy_stream, m->ev_consumed[slot], 0));
+  } else {
+    // A pageable copy waits, on the host and without a bound, for the copy
+    // stream's earlier work: make both waits bounded first.
+    ORCA_TRY(wait_event_for(m->ev_consumed[slot], ctx->sync_timeout_s));
+    ORCA_TRY(sync_stream_for(ctx, m->copy_stream, ctx->sync_timeout_s));
+  }
+  const size_t xb = (size_t)(m->B * m->dims[0]) * 4, tb = (size_t)(m->B * m->dims[m->L]) * 4;
+  ORCA_CUDA_TRY(cudaMemcpyAsync(m->slot_x[slot], x, xb, cudaMemcpyHostToDevice, m->copy_stream));
+  ORCA_CUDA_TRY(cudaMemcpyAsync(m->slot_t[slot], t, tb, cudaMemcpyHostToDevice, m->copy_stream));
+  ORCA_CUDA_TRY(cudaEventRecord(m->ev_staged[slot], m->copy_stream));
+  m->slot_ready[slot] = true;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_step_staged(orca_mlp* m, int slot, float* loss) {
+  if (!m) return fail(ORCA_INVALID_ARGUMENT, "null mlp");
+  if (slot < 0 || slot >= ORCA_MLP_STAGE_SLOTS)
+    return fail(ORCA_INVALID_ARGUMENT, "slot must be in [0, %d)", ORCA_MLP_STAGE_SLOTS);
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  if (!m->slot_ready[slot])
+    return fail(ORCA_INVALID_ARGUMENT, "slot %d holds no staged batch", slot);
+  ORCA_CUDA_TRY(cudaStreamWaitEvent(m->ctx->stream, m->ev_staged[slot], 0));
+  m->slot_ready[slot] = false;
+  ORCA_TRY(step_device_locked(m, m->slot_x[slot], m->slot_t[slot], nullptr,
+                              m->ev_consumed[slot]));
+  if (loss) return read_loss_locked(m, loss);
   return ORCA_OK;
 }
 

@@ -99,9 +99,13 @@ orca_status sync_stream(orca_ctx* ctx) {
 
 orca_status sync_stream_for(orca_ctx* ctx, cudaStream_t stream, double timeout_s) {
   ORCA_CUDA_TRY(cudaEventRecord(ctx->sync_event, stream));
+  return wait_event_for(ctx->sync_event, timeout_s);
+}
+
+orca_status wait_event_for(cudaEvent_t event, double timeout_s) {
   const auto t0 = std::chrono::steady_clock::now();
   for (int it = 0;; ++it) {
-    const cudaError_t e = cudaEventQuery(ctx->sync_event);
+    const cudaError_t e = cudaEventQuery(event);
     if (e == cudaSuccess) return ORCA_OK;
     if (e != cudaErrorNotReady)
       return fail(ORCA_CUDA_ERROR, "stream error: %s", cudaGetErrorString(e));
@@ -459,6 +463,25 @@ orca_status orca_ctx_device(const orca_ctx* ctx, int* device) {
 }
 
 void* orca_ctx_stream(orca_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+orca_status orca_host_alloc(size_t bytes, void** out) {
+  if (!out || !bytes) return fail(ORCA_INVALID_ARGUMENT, "host_alloc: null output or zero size");
+  *out = nullptr;
+  const cudaError_t e = cudaHostAlloc(out, bytes, cudaHostAllocPortable);
+  if (e != cudaSuccess) {
+    *out = nullptr;
+    return fail(ORCA_CUDA_ERROR, "page-locked allocation of %zu bytes failed: %s", bytes,
+                cudaGetErrorString(e));
+  }
+  return ORCA_OK;
+}
+
+orca_status orca_host_free(void* ptr) {
+  if (!ptr) return ORCA_OK;
+  const cudaError_t e = cudaFreeHost(ptr);
+  if (e != cudaSuccess) return fail(ORCA_CUDA_ERROR, "host_free: %s", cudaGetErrorString(e));
+  return ORCA_OK;
+}
 
 uint64_t orca_ctx_launch_count(const orca_ctx* ctx) { return ctx ? ctx->launches.load() : 0; }
 

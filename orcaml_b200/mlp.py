@@ -250,6 +250,23 @@ class MlpTrainer:
         L.check(L.load().orca_mlp_step_device(self._h, ctypes.c_void_p(x_dev), ctypes.c_void_p(t_dev),
                                               ctypes.c_void_p(loss_dev) if loss_dev else None))
 
+    def stage_batch(self, slot: int, x, t):
+        """Copy a batch into device slot `slot` (0 or 1) on the step runner's
+        copy stream.  With page-locked x and t (dataloader.pinned_empty) the
+        call returns at once and the arrays must stay unchanged until the
+        step on that slot has returned; pageable arrays are copied before it
+        returns."""
+        x, t = self._check_batch(x, t)
+        L.check(L.load().orca_mlp_stage_batch(self._h, int(slot),
+                                              x.ctypes.data_as(ctypes.c_void_p),
+                                              t.ctypes.data_as(ctypes.c_void_p)))
+
+    def step_staged(self, slot: int) -> float:
+        """One training step on the batch staged in `slot`; returns the loss."""
+        loss = ctypes.c_float()
+        L.check(L.load().orca_mlp_step_staged(self._h, int(slot), ctypes.byref(loss)))
+        return float(loss.value)
+
     def graph_capture(self, x_dev: int, t_dev: int, loss_dev: int = 0):
         """Record one step on fixed device buffers as a CUDA graph (SGD, no
         communicator); graph_step() then replays it with one launch."""
