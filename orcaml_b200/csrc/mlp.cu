@@ -131,66 +131,145 @@ struct SgdArgs {
   int use_wd, use_mom, use_damp, first;
 };
 
-// SGD.step (python/orca/optim/sgd.py:55-79), one rounding per reference op.
-// p is (hi, lo) planes when lo != nullptr, else plain fp32 in hi.
-__global__ void sgd_kernel(float* __restrict__ hi, float* __restrict__ lo,
-                           const float* __restrict__ g, float* __restrict__ v, int64_t n,
-                           SgdArgs a) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    float p = lo ? __fadd_rn(hi[i], lo[i]) : hi[i];
-    float gi = g[i];
-    if (a.use_wd) gi = __fadd_rn(gi, __fmul_rn(p, a.wd));
-    if (a.use_mom) {
-      float vi;
-      if (a.first) vi = gi;
-      else if (a.use_damp) vi = __fadd_rn(__fmul_rn(v[i], a.mom), __fmul_rn(gi, a.one_minus_damp));
-      else vi = __fadd_rn(__fmul_rn(v[i], a.mom), gi);
-      v[i] = vi;
-      gi = vi;
-    }
-    p = __fsub_rn(p, __fmul_rn(gi, a.lr));
-    if (lo) {
-      float h, l;
-      split_tf32(p, h, l);
-      hi[i] = h;
-      lo[i] = l;
-    } else {
-      hi[i] = p;
-    }
+// SGD.step (python/orca/optim/sgd.py:55-79) of one parameter, one rounding per
+// reference op.  v (the velocity) is read only after the first momentum step
+// and written whenever momentum is on.
+__device__ __forceinline__ float sgd_elem(float p, float gi, float& v, const SgdArgs& a) {
+  if (a.use_wd) gi = __fadd_rn(gi, __fmul_rn(p, a.wd));
+  if (a.use_mom) {
+    if (a.first) v = gi;
+    else if (a.use_damp) v = __fadd_rn(__fmul_rn(v, a.mom), __fmul_rn(gi, a.one_minus_damp));
+    else v = __fadd_rn(__fmul_rn(v, a.mom), gi);
+    gi = v;
   }
+  return __fsub_rn(p, __fmul_rn(gi, a.lr));
 }
 
 struct AdamArgs {
   float decay, b1, one_minus_b1, b2, one_minus_b2, bc1, bc2, eps, lr;
 };
 
-// AdamW.step (python/orca/optim/adamw.py:75-99), one rounding per reference op.
+// AdamW.step (python/orca/optim/adamw.py:75-99) of one parameter, one rounding
+// per reference op; m and v are updated in place.
+__device__ __forceinline__ float adamw_elem(float p, float gi, float& m, float& v,
+                                            const AdamArgs& a) {
+  const float decayed = __fmul_rn(p, a.decay);
+  m = __fadd_rn(__fmul_rn(m, a.b1), __fmul_rn(gi, a.one_minus_b1));
+  v = __fadd_rn(__fmul_rn(v, a.b2), __fmul_rn(__fmul_rn(gi, gi), a.one_minus_b2));
+  const float mh = __fmul_rn(m, a.bc1);
+  const float vh = __fmul_rn(v, a.bc2);
+  const float denom = __fadd_rn(__fsqrt_rn(vh), a.eps);
+  return __fsub_rn(decayed, __fmul_rn(__fdiv_rn(mh, denom), a.lr));
+}
+
+// p is (hi, lo) planes when kPlanes, else plain fp32 in hi.
+template <bool kPlanes>
+__device__ __forceinline__ float load_param(const float* hi, const float* lo, int64_t i) {
+  return kPlanes ? __fadd_rn(hi[i], lo[i]) : hi[i];
+}
+
+template <bool kPlanes>
+__device__ __forceinline__ void store_param(float* hi, float* lo, int64_t i, float p) {
+  if (kPlanes) {
+    float h, l;
+    split_tf32(p, h, l);
+    hi[i] = h;
+    lo[i] = l;
+  } else {
+    hi[i] = p;
+  }
+}
+
+// Four consecutive parameters per thread and iteration as 128-bit accesses
+// (every array 16-byte aligned); the n % 4 tail goes element by element.
+template <bool kPlanes>
+__device__ __forceinline__ void load_param4(const float* hi, const float* lo, int64_t q,
+                                            float (&p)[4]) {
+  const float4 h = reinterpret_cast<const float4*>(hi)[q];
+  p[0] = h.x; p[1] = h.y; p[2] = h.z; p[3] = h.w;
+  if (kPlanes) {
+    const float4 l = reinterpret_cast<const float4*>(lo)[q];
+    p[0] = __fadd_rn(p[0], l.x); p[1] = __fadd_rn(p[1], l.y);
+    p[2] = __fadd_rn(p[2], l.z); p[3] = __fadd_rn(p[3], l.w);
+  }
+}
+
+template <bool kPlanes>
+__device__ __forceinline__ void store_param4(float* hi, float* lo, int64_t q, const float (&p)[4]) {
+  if (kPlanes) {
+    float h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) split_tf32(p[j], h[j], l[j]);
+    reinterpret_cast<float4*>(hi)[q] = make_float4(h[0], h[1], h[2], h[3]);
+    reinterpret_cast<float4*>(lo)[q] = make_float4(l[0], l[1], l[2], l[3]);
+  } else {
+    reinterpret_cast<float4*>(hi)[q] = make_float4(p[0], p[1], p[2], p[3]);
+  }
+}
+
+__device__ __forceinline__ void to4(const float4 v, float (&o)[4]) {
+  o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+}
+
+template <bool kPlanes, bool kVec>
+__global__ void sgd_kernel(float* __restrict__ hi, float* __restrict__ lo,
+                           const float* __restrict__ g, float* __restrict__ v, int64_t n,
+                           SgdArgs a) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool read_v = a.use_mom && !a.first;
+  int64_t tail = 0;
+  if (kVec) {
+    const int64_t n4 = n >> 2;
+    for (int64_t q = t0; q < n4; q += stride) {
+      float p[4], gv[4], vv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      load_param4<kPlanes>(hi, lo, q, p);
+      to4(reinterpret_cast<const float4*>(g)[q], gv);
+      if (read_v) to4(reinterpret_cast<const float4*>(v)[q], vv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[j] = sgd_elem(p[j], gv[j], vv[j], a);
+      if (a.use_mom) reinterpret_cast<float4*>(v)[q] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      store_param4<kPlanes>(hi, lo, q, p);
+    }
+    tail = n4 << 2;
+  }
+  for (int64_t i = tail + t0; i < n; i += stride) {
+    float vi = read_v ? v[i] : 0.0f;
+    const float p = sgd_elem(load_param<kPlanes>(hi, lo, i), g[i], vi, a);
+    if (a.use_mom) v[i] = vi;
+    store_param<kPlanes>(hi, lo, i, p);
+  }
+}
+
+template <bool kPlanes, bool kVec>
 __global__ void adamw_kernel(float* __restrict__ hi, float* __restrict__ lo,
                              const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, int64_t n, AdamArgs a) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float p = lo ? __fadd_rn(hi[i], lo[i]) : hi[i];
-    const float gi = g[i];
-    const float decayed = __fmul_rn(p, a.decay);
-    const float mi = __fadd_rn(__fmul_rn(m[i], a.b1), __fmul_rn(gi, a.one_minus_b1));
-    const float vi = __fadd_rn(__fmul_rn(v[i], a.b2), __fmul_rn(__fmul_rn(gi, gi), a.one_minus_b2));
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t tail = 0;
+  if (kVec) {
+    const int64_t n4 = n >> 2;
+    for (int64_t q = t0; q < n4; q += stride) {
+      float p[4], gv[4], mv[4], vv[4];
+      load_param4<kPlanes>(hi, lo, q, p);
+      to4(reinterpret_cast<const float4*>(g)[q], gv);
+      to4(reinterpret_cast<const float4*>(m)[q], mv);
+      to4(reinterpret_cast<const float4*>(v)[q], vv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[j] = adamw_elem(p[j], gv[j], mv[j], vv[j], a);
+      reinterpret_cast<float4*>(m)[q] = make_float4(mv[0], mv[1], mv[2], mv[3]);
+      reinterpret_cast<float4*>(v)[q] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      store_param4<kPlanes>(hi, lo, q, p);
+    }
+    tail = n4 << 2;
+  }
+  for (int64_t i = tail + t0; i < n; i += stride) {
+    float mi = m[i], vi = v[i];
+    const float p = adamw_elem(load_param<kPlanes>(hi, lo, i), g[i], mi, vi, a);
     m[i] = mi;
     v[i] = vi;
-    const float mh = __fmul_rn(mi, a.bc1);
-    const float vh = __fmul_rn(vi, a.bc2);
-    const float denom = __fadd_rn(__fsqrt_rn(vh), a.eps);
-    const float upd = __fmul_rn(__fdiv_rn(mh, denom), a.lr);
-    const float np = __fsub_rn(decayed, upd);
-    if (lo) {
-      float h, l;
-      split_tf32(np, h, l);
-      hi[i] = h;
-      lo[i] = l;
-    } else {
-      hi[i] = np;
-    }
+    store_param<kPlanes>(hi, lo, i, p);
   }
 }
 
@@ -230,6 +309,74 @@ static AdamArgs adam_args(double lr, double b1, double b2, double eps, double wd
 
 static int ew_grid(orca_ctx* ctx, int64_t n) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(n, 256), (int64_t)ctx->sm_count * 8));
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// The optimizer kernels take the 128-bit form when every array they touch is
+// 16-byte aligned (parameters, gradients and state of the step runner are,
+// except after a parameter whose size is not a multiple of 4).
+// Resident 256-thread blocks per SM of a kernel (its register use decides).
+template <typename Kernel>
+static int blocks_per_sm(Kernel kernel) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  return per_sm;
+}
+
+// Grid of a grid-stride kernel: one wave of resident blocks, fewer for small
+// n.  A second, partial wave would leave SMs idle while it runs.
+static int resident_grid(orca_ctx* ctx, int per_sm, int64_t items) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(items, 256),
+                                                     (int64_t)ctx->sm_count * per_sm));
+}
+
+template <bool kPlanes, bool kVec>
+static void launch_sgd_as(orca_ctx* ctx, float* hi, float* lo, const float* g, float* v, int64_t n,
+                          const SgdArgs& a) {
+  static const int per_sm = blocks_per_sm(sgd_kernel<kPlanes, kVec>);
+  const int grid = resident_grid(ctx, per_sm, kVec ? cdiv(n, 4) : n);
+  sgd_kernel<kPlanes, kVec><<<grid, 256, 0, ctx->stream>>>(hi, lo, g, v, n, a);
+}
+
+template <bool kPlanes, bool kVec>
+static void launch_adamw_as(orca_ctx* ctx, float* hi, float* lo, const float* g, float* m,
+                            float* v, int64_t n, const AdamArgs& a) {
+  static const int per_sm = blocks_per_sm(adamw_kernel<kPlanes, kVec>);
+  const int grid = resident_grid(ctx, per_sm, kVec ? cdiv(n, 4) : n);
+  adamw_kernel<kPlanes, kVec><<<grid, 256, 0, ctx->stream>>>(hi, lo, g, m, v, n, a);
+}
+
+static void launch_sgd(orca_ctx* ctx, float* hi, float* lo, const float* g, float* v, int64_t n,
+                       const SgdArgs& a) {
+  const bool vec = aligned16(hi) && (!lo || aligned16(lo)) && aligned16(g) &&
+                   (!v || aligned16(v));
+  if (lo) {
+    if (vec) launch_sgd_as<true, true>(ctx, hi, lo, g, v, n, a);
+    else launch_sgd_as<true, false>(ctx, hi, lo, g, v, n, a);
+  } else {
+    if (vec) launch_sgd_as<false, true>(ctx, hi, lo, g, v, n, a);
+    else launch_sgd_as<false, false>(ctx, hi, lo, g, v, n, a);
+  }
+  count_launch(ctx);
+}
+
+static void launch_adamw(orca_ctx* ctx, float* hi, float* lo, const float* g, float* m, float* v,
+                         int64_t n, const AdamArgs& a) {
+  const bool vec = aligned16(hi) && (!lo || aligned16(lo)) && aligned16(g) && aligned16(m) &&
+                   aligned16(v);
+  if (lo) {
+    if (vec) launch_adamw_as<true, true>(ctx, hi, lo, g, m, v, n, a);
+    else launch_adamw_as<true, false>(ctx, hi, lo, g, m, v, n, a);
+  } else {
+    if (vec) launch_adamw_as<false, true>(ctx, hi, lo, g, m, v, n, a);
+    else launch_adamw_as<false, false>(ctx, hi, lo, g, m, v, n, a);
+  }
+  count_launch(ctx);
 }
 
 // g[i] = mask[i] > 0 ? g[i] : 0 (one comparison, no arithmetic: bit-exact).
@@ -1237,14 +1384,12 @@ static orca_status mlp_update_impl(orca_mlp* m) {
       const float* g = m->grads + m->p_off[idx];
       if (m->opt == ORCA_OPT_SGD) {
         float* v = m->state0 ? m->state0 + m->p_off[idx] : nullptr;
-        SgdArgs a = sgd_args(m->lr, m->mom, m->damp, m->wd, m->vel_init ? 0 : 1);
-        sgd_kernel<<<ew_grid(ctx, n), 256, 0, ctx->stream>>>(hi, lo, g, v, n, a);
+        launch_sgd(ctx, hi, lo, g, v, n,
+                   sgd_args(m->lr, m->mom, m->damp, m->wd, m->vel_init ? 0 : 1));
       } else {
-        AdamArgs a = adam_args(m->lr, m->b1, m->b2, m->eps, m->wd, m->t);
-        adamw_kernel<<<ew_grid(ctx, n), 256, 0, ctx->stream>>>(
-            hi, lo, g, m->state0 + m->p_off[idx], m->state1 + m->p_off[idx], n, a);
+        launch_adamw(ctx, hi, lo, g, m->state0 + m->p_off[idx], m->state1 + m->p_off[idx], n,
+                     adam_args(m->lr, m->b1, m->b2, m->eps, m->wd, m->t));
       }
-      count_launch(ctx);
     }
   }
   prof_close(m, pr);
@@ -1469,11 +1614,8 @@ orca_status orca_sgd_step(orca_ctx* ctx, orca_buf* p, const orca_buf* g, orca_bu
   if (g->n != p->n || (v && v->n != p->n)) return fail(ORCA_SHAPE_MISMATCH, "sgd_step: sizes");
   if (momentum != 0.0 && !v) return fail(ORCA_INVALID_ARGUMENT, "sgd_step: momentum needs v");
   const int64_t n = (int64_t)p->n;
-  SgdArgs a = sgd_args(lr, momentum, dampening, weight_decay, first);
-  sgd_kernel<<<ew_grid(ctx, n), 256, 0, ctx->stream>>>((float*)p->ptr, nullptr,
-                                                       (const float*)g->ptr,
-                                                       v ? (float*)v->ptr : nullptr, n, a);
-  count_launch(ctx);
+  launch_sgd(ctx, (float*)p->ptr, nullptr, (const float*)g->ptr, v ? (float*)v->ptr : nullptr, n,
+             sgd_args(lr, momentum, dampening, weight_decay, first));
   ORCA_CUDA_TRY(cudaGetLastError());
   return ORCA_OK;
 }
@@ -1488,11 +1630,8 @@ orca_status orca_adamw_step(orca_ctx* ctx, orca_buf* p, const orca_buf* g, orca_
     return fail(ORCA_SHAPE_MISMATCH, "adamw_step: sizes");
   if (t < 1) return fail(ORCA_INVALID_ARGUMENT, "adamw_step: t starts at 1");
   const int64_t n = (int64_t)p->n;
-  AdamArgs a = adam_args(lr, beta1, beta2, eps, weight_decay, t);
-  adamw_kernel<<<ew_grid(ctx, n), 256, 0, ctx->stream>>>((float*)p->ptr, nullptr,
-                                                         (const float*)g->ptr, (float*)m->ptr,
-                                                         (float*)v->ptr, n, a);
-  count_launch(ctx);
+  launch_adamw(ctx, (float*)p->ptr, nullptr, (const float*)g->ptr, (float*)m->ptr,
+               (float*)v->ptr, n, adam_args(lr, beta1, beta2, eps, weight_decay, t));
   ORCA_CUDA_TRY(cudaGetLastError());
   return ORCA_OK;
 }

@@ -175,6 +175,24 @@ def test_adamw_matches_oracle(be):
     tr.close()
 
 
+@pytest.mark.parametrize("opt,kw", [("sgd", dict(lr=0.05, momentum=0.9, weight_decay=0.01)),
+                                    ("adamw", dict(lr=1e-3, weight_decay=0.01))])
+def test_odd_parameter_sizes_match_oracle(be, opt, kw):
+    """Parameter sizes that are not multiples of 4: the weight planes and the
+    gradient offsets after them are not 16-byte aligned, so the optimizer
+    takes its element-by-element form; 5 steps on a ragged batch."""
+    dims, B = [13, 7, 5, 3], 9
+    x, t, _ = make_batch(dims, B, 0)
+    tr = make(be, dims, B, opt, **kw)
+    ref = oracle_trainer(dims, opt, **kw)
+    for step in range(5):
+        lg, lr_ = tr.step(x, t), ref.step(x, t)
+        assert abs(lg - lr_) <= TOL * abs(lr_), (step, lg, lr_)
+    for p, q in zip(tr.get_parameters(), ref.params):
+        assert rel_err(p, q) <= TOL
+    tr.close()
+
+
 def test_c2_width_reduced_batch_matches_oracle(be):
     """configs[2]'s model (784-8192-8192-10, SGD momentum 0.9, lr 0.01) with a
     256-row batch so the oracle finishes in seconds: 2 steps."""
