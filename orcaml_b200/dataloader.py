@@ -359,6 +359,8 @@ class DataLoader:
         for i, s in enumerate(norm[1:], start=1):
             if len(s) != arity:
                 raise ValueError(f"Sample at index {i} has {len(s)} fields, expected {arity}")
+        if out is not None and len(out) != arity:
+            raise ValueError(f"samples have {arity} fields, the staging buffers {len(out)}")
         fields = []
         for f in range(arity):
             values = [s[f] for s in norm]
@@ -380,6 +382,9 @@ class DataLoader:
     def _gather(self, rows, batch: List[int], out: Optional[List[np.ndarray]] = None):
         """An ArrayDataset batch as one row gather per field."""
         base, index_map = rows
+        if out is not None and len(out) != len(base.arrays):
+            raise ValueError(f"samples have {len(base.arrays)} fields, the staging buffers "
+                             f"{len(out)}")
         idx = np.asarray(batch, np.int64)
         if index_map is not None:
             idx = index_map[idx]
@@ -496,9 +501,7 @@ class StagedFeeder:
                             break
                         except queue.Empty:
                             continue
-                    fields, _ = next(it)
-                    if len(fields) != 2:
-                        raise ValueError("training batches must be (inputs, targets) pairs")
+                    next(it)
                     ready.put(slot_of[0])
                 ready.put(done)
             except BaseException as exc:   # handed to the training thread

@@ -217,3 +217,8 @@ def test_staged_feeder_rejects_mismatch_and_reports_worker_errors():
                             host_alloc=alloc)
     with pytest.raises(ValueError, match="bad sample"):
         feeder.run()
+    three = D.ArrayDataset(np.zeros((4, 5)), np.zeros((4, 3)), np.zeros((4, 1)))
+    feeder = D.StagedFeeder(_LateCopyTrainer([5, 3], 2), D.DataLoader(three, batch_size=2),
+                            host_alloc=alloc)
+    with pytest.raises(ValueError, match="fields"):
+        feeder.run()
