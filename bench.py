@@ -320,10 +320,11 @@ def run_ours(args):
     tc_flops = sum(s["flops"] * s["launches"] for s in tc_sites)
     tc_launches = sum(s["launches"] for s in tc_sites)
     # DRAM read + write of one tcgen05 GEMM launch, from an ncu --set full
-    # capture (profiles/tc_gemm_kdot_c2_fwd_l1.md) of the configs[2] forward
-    # product of the 8192x8192 layer (M=4096, N=8192, K=8192, with the
-    # classifier dot): 2.903 GB read + 0.265 GB written; its algorithmic
-    # operand + output bytes are 1.09 GB.  Other configs: not captured.
+    # capture of the configs[2] forward product of the 8192x8192 layer
+    # (M=4096, N=8192, K=8192, with the classifier dot; the kDot launch of
+    # `python bench.py --steps 3 --warmup 3 --no-cpu`): 2.903 GB read +
+    # 0.265 GB written; its algorithmic operand + output bytes are 1.09 GB.
+    # Other configs: not captured.
     traffic = {"bytes_per_launch": 3.168e9, "launch": "configs[2] forward 4096x8192x8192 (+dot)",
                "algorithmic_bytes": 1.087e9} if CFG.name == "c2" else None
     achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else 0.0

@@ -8,9 +8,9 @@
  * `GpuBackend` (orca-backend-gpu, wgpu), wrapped by `Autodiff<B>` and exposed
  * to Python by the PyO3 module `orca.orca_python` (orca-python/src/lib.rs).
  * A Rust `orca-backend-cuda` crate implements `Backend` by calling the
- * `orca_*` functions below one-to-one (see INTEGRATION.md for the binding);
- * the Python host layer of this repository (orcaml_b200) binds the same
- * symbols through ctypes.
+ * `orca_*` functions below one-to-one (each storage an Arc'd handle whose
+ * Drop calls orca_buf_release); the Python host layer of this repository
+ * (orcaml_b200) binds the same symbols through ctypes.
  *
  * Conventions
  *  - Every function returns an orca_status; ORCA_OK is 0.  The message of
