@@ -159,6 +159,21 @@ def cpu_baseline(steps=1, batch=64, warmup=0):
             "seconds": dt}
 
 
+def socket_ddp_baseline(world=2, sample=1 << 20):
+    """The reference's socket gradient exchange (oracle/socket_ddp.py restates
+    python/orca/distributed.py:65-256: a star through rank 0, Python lists
+    averaged in doubles) timed on this host: `world` local processes exchange
+    one `sample`-float gradient; the per-step figure scales that to the
+    configuration's parameter count (the exchange is linear in the element
+    count: byte streams and per-element Python loops)."""
+    from oracle import socket_ddp as S
+    dt, _, _ = S.run(world, [sample])
+    return {"world": world, "sample_floats": sample, "sample_s": dt,
+            "per_step_s": dt * CFG.n_params / sample, "kind": "port",
+            "sample": f"{world} processes on 127.0.0.1 exchanging one {sample}-float gradient; "
+                      f"per step = x {CFG.n_params} / {sample} parameters"}
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -174,6 +189,9 @@ def run_reference(args):
     t0 = time.perf_counter()
     cpu_baseline(steps=max(args.warmup, 0), batch=batch) if args.warmup else None
     res = cpu_baseline(steps=args.steps, batch=batch)
+    # At N > 1 the reference's job also exchanges every gradient over its
+    # sockets each step: timed separately at the same world size.
+    ddp = socket_ddp_baseline(world=args.gpus) if args.gpus > 1 else None
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * res["seconds"] / args.steps, "higher_is_better": True,
@@ -181,7 +199,8 @@ def run_reference(args):
             "config": {"workload": describe(CFG) + f"; CPU, bounded sample of {batch} rows "
                                                    "per step",
                        "global_batch": batch, "parallelism": "single process (rank 0)"},
-            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": dict({k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                                 socket_ddp=ddp),
             "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "wall_s": time.perf_counter() - t0}
@@ -372,6 +391,7 @@ def run_ours(args):
         }
         if cpu is not None:
             result["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            result["cpu_baseline"]["socket_ddp"] = socket_ddp_baseline()
         print(json.dumps(result), flush=True)
     if comm is not None:
         tr.attach_comm(None)

@@ -38,3 +38,15 @@ def test_reference_arm_non_zero_rank_exits_quietly():
                           "--steps", "1", "--warmup", "0"], capture_output=True, text=True,
                          timeout=300, cwd=REPO, env=dict(os.environ, WORLD_SIZE="2", RANK="1"))
     assert out.returncode == 0 and not out.stdout.strip()
+
+
+def test_reference_arm_at_two_gpus_times_the_socket_exchange():
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "0", "--gpus", "2", "--config", "c0"],
+                         capture_output=True, text=True, timeout=600, cwd=REPO,
+                         env=dict(os.environ, WORLD_SIZE="2", RANK="0"))
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads([ln for ln in out.stdout.splitlines() if ln.startswith("{")][0])
+    ddp = d["cpu_baseline"]["socket_ddp"]
+    assert ddp["world"] == 2 and ddp["kind"] == "port"
+    assert ddp["sample_s"] > 0 and ddp["per_step_s"] > ddp["sample_s"] * 0.5

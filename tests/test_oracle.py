@@ -204,3 +204,19 @@ def test_oracle_order_sensitivity():
     assert max(abs(a - b) / b for a, b in zip(l0, l1)) < 1e-4
     worst = max(float(np.linalg.norm(a - b) / np.linalg.norm(b)) for a, b in zip(p0, p1))
     assert worst > 1e-4
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_socket_exchange_port_averages_like_the_oracle(world):
+    """oracle/socket_ddp.py (the reference's socket star, timed by bench.py's
+    CPU-baseline leg) returns, bit for bit, the DDP average the oracle
+    restates and the golden DDP fixture pins."""
+    from oracle import socket_ddp as S
+    sizes = [5, 1000, 3, 0]
+    _, out, inputs = S.run(world, sizes, seed=11)
+    for j, n in enumerate(sizes):
+        if n == 0:
+            assert out[j].size == 0
+            continue
+        ref = O.ddp_average([inputs[r][j] for r in range(world)])
+        assert np.array_equal(out[j], ref)
