@@ -17,8 +17,16 @@ device synchronise on both sides, timed with CUDA events on the library's
 compute stream, max over ranks.  The step's working set (the 8192x8192
 weight planes alone are 512 MB) exceeds the 126 MB L2, so no flush is needed.
 
+At N > 1 every rank first runs a data-parallel parity pre-check outside the
+timed region (`ddp_parity` in the JSON line; `--no-parity` skips it): a
+reduced model through the same trainer and NCCL communicator, against the
+oracle's restatement of the reference's DDP average.
+
 `--impl reference` times the reference's CPU path restated in oracle/ (the
-Rust reference cannot be built here) on the host cores, rank 0 only.
+Rust reference cannot be built here) on the host cores, rank 0 only, with a
+packed FMA GEMM standing in for the reference's matrixmultiply crate; steps
+are timed on 128- and 512-row samples and `value` is their fixed + per-row
+fit at the configuration's batch.
 """
 from __future__ import annotations
 
@@ -133,30 +141,89 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(steps=1, batch=64, warmup=0):
+def _fit(points):
+    """Least-squares fixed + per-row cost from (rows, seconds) points."""
+    xs = np.array([r for r, _ in points], np.float64)
+    ys = np.array([t for _, t in points], np.float64)
+    if len(set(xs.tolist())) < 2:
+        return None
+    per_row, fixed = np.polyfit(xs, ys, 1)
+    return {"fixed_s": float(fixed), "per_row_ms": float(per_row * 1e3)}
+
+
+def cpu_gemm_gflops():
+    """GFLOP/s of the timing GEMM (packed FMA kernel, one thread) on a slab
+    of the configs' widest product: [256, 8192] x [8192, 1024]."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    a = rng.random((256, 8192), dtype=np.float32)
+    b = rng.random((8192, 1024), dtype=np.float32)
+    O.sgemm_packed(a[:64], b[:, :256])          # page in
+    t0 = time.perf_counter()
+    ok = O.sgemm_packed(a, b) is not None
+    dt = time.perf_counter() - t0
+    return 2.0 * 256 * 8192 * 1024 / dt / 1e9 if ok else None
+
+
+def cpu_step_times(batches):
     """The reference's CPU path (oracle/, restating orca-backend-cpu + the
-    Python frontend) on a bounded sample: `batch` rows of the configs[2]
-    model per step, all host threads for the element-wise loops, the GEMM
-    single-threaded like the reference's matrixmultiply."""
+    Python frontend) timed one step per entry of `batches` (rows per step) on
+    the configuration's model: element-wise loops on all host threads (the
+    reference's rayon maps), the GEMM single-threaded on the packed FMA
+    kernel that stands in for the reference's matrixmultiply (the oracle's
+    parity GEMM is a plain loop ~4x slower; it is not what the reference
+    runs).  The first step (velocity allocation) is run untimed."""
     from oracle import oracle as O
     O.set_threads(0)
+    O.set_gemm_threads(1)
+    O.set_gemm_order(4)
     dims = CFG.dims
     kw = opt_kwargs(CFG)
     kw.pop("betas", None), kw.pop("eps", None)
     tr = O.OracleTrainer(dims, init_params(dims, 1), optimizer=CFG.optimizer, **kw)
-    x, t, _ = make_batch(dims, batch, 0, CFG.inputs)
-    for _ in range(warmup):
-        tr.step(x, t)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        tr.step(x, t)
-    dt = time.perf_counter() - t0
-    return {"value": steps * batch / dt, "unit": UNIT, "cores": O.threads(),
-            "kind": "port",
-            "sample": f"{steps} step(s) of the {'-'.join(str(d) for d in dims)} {CFG.optimizer} "
-                      f"step at batch {batch} (of {CFG.batch}): GEMM single-threaded, element-wise "
-                      f"loops on {O.threads()} threads",
-            "seconds": dt}
+    xs = {}
+    for b in sorted(set(batches)):
+        x, t, _ = make_batch(dims, b, 0, CFG.inputs)
+        xs[b] = (x, t)
+    tr.step(*xs[min(xs)])
+    out = []
+    for b in batches:
+        t0 = time.perf_counter()
+        tr.step(*xs[b])
+        out.append((b, time.perf_counter() - t0))
+    O.set_gemm_order(0)
+    return out, O.threads()
+
+
+def sample_rows():
+    """Rows of the CPU samples: 512 and 128, or the configuration's batch and
+    a quarter of it when that is smaller."""
+    big = min(512, CFG.batch)
+    return big, max(1, big // 4)
+
+
+def cpu_baseline_from(points, cores, label):
+    """cpu_baseline object: the measured rate of the largest sample, and the
+    fixed + per-row fit of all samples extrapolated to the configuration's
+    per-rank batch (the fixed part -- transposes, optimizer passes over every
+    parameter -- is paid once per step, so small samples understate the
+    reference's rate at the full batch)."""
+    fit = _fit(points)
+    big = max(r for r, _ in points)
+    tb = [t for r, t in points if r == big]
+    measured = big / statistics.median(tb)
+    full = None
+    if fit and fit["per_row_ms"] > 0:
+        full = CFG.batch / (max(fit["fixed_s"], 0.0) + CFG.batch * fit["per_row_ms"] / 1e3)
+    gf = cpu_gemm_gflops()
+    return {"value": full if full else measured, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{label}; value = fixed + per-row fit of the timed steps extrapolated to "
+                      f"the {CFG.batch}-row batch (measured {measured:.2f} samples/s at {big} rows)",
+            "measured_value": measured, "measured_rows": big,
+            "fit": fit, "points": [[r, round(t, 4)] for r, t in points],
+            "gemm_gflops": gf,
+            "gemm": "packed 8x8 FMA micro-kernel, KC 256 / MC 64 / NC 1024, one thread "
+                    "(matrixmultiply 0.3's design, default features)"}
 
 
 def socket_ddp_baseline(world=2, sample=1 << 20):
@@ -182,30 +249,119 @@ def dist_env():
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU path on the host cores (the
+    Rust reference cannot be built here, so its restatement in oracle/ runs),
+    rank 0 only.  Warm-up steps run on 128-row samples and timed steps on
+    512-row samples (both timed one by one for the fit); `value` is the fit
+    extrapolated to the configuration's batch.  At N > 1 every step of the
+    reference's DDP job also exchanges every gradient through its socket
+    star (timed at world N on this host and added per step)."""
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    batch = 64
     t0 = time.perf_counter()
-    cpu_baseline(steps=max(args.warmup, 0), batch=batch) if args.warmup else None
-    res = cpu_baseline(steps=args.steps, batch=batch)
-    # At N > 1 the reference's job also exchanges every gradient over its
-    # sockets each step: timed separately at the same world size.
+    big, small = sample_rows()
+    pts, cores = cpu_step_times([small] * max(2, args.warmup) + [big] * max(1, args.steps))
+    res = cpu_baseline_from(pts, cores, f"{max(1, args.steps)} step(s) at {big} rows and "
+                                        f"{max(2, args.warmup)} at {small} rows of the "
+                                        f"{'-'.join(str(d) for d in CFG.dims)} {CFG.optimizer} "
+                                        f"step: GEMM one thread, element-wise loops on {cores} "
+                                        "threads")
+    step_s = CFG.batch / res["value"]
     ddp = socket_ddp_baseline(world=args.gpus) if args.gpus > 1 else None
-    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
+    if ddp:
+        step_s += ddp["per_step_s"]
+    value = args.gpus * CFG.batch / step_s
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * res["seconds"] / args.steps, "higher_is_better": True,
+            "ms_per_step": 1000.0 * step_s, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": describe(CFG) + f"; CPU, bounded sample of {batch} rows "
-                                                   "per step",
-                       "global_batch": batch, "parallelism": "single process (rank 0)"},
-            "cpu_baseline": dict({k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
-                                 socket_ddp=ddp),
-            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+            "config": {"workload": describe(CFG) + "; CPU; per-rank step time = fixed + per-row "
+                                                   f"fit of timed {small}- and {big}-row steps at the "
+                                                   f"{CFG.batch}-row batch"
+                                                   + (f", plus the socket exchange at world "
+                                                      f"{args.gpus}" if ddp else ""),
+                       "global_batch": args.gpus * CFG.batch, "per_rank_batch": CFG.batch,
+                       "timed_rows_per_step": big,
+                       "parallelism": "single process (rank 0)" if args.gpus == 1 else
+                       f"rank 0 computes; {args.gpus} ranks assumed, each with the host to itself"},
+            "cpu_baseline": dict(res, value=value, socket_ddp=ddp),
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "wall_s": time.perf_counter() - t0}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def ddp_parity_check(be, world, rank, dist, local):
+    """Data-parallel parity before the timed run (outside it): a reduced
+    model (784-1024-1024-10, 512 rows per rank, SGD momentum 0.9, lr 0.01)
+    on the tensor-core path through the same trainer and NCCL communicator
+    as the timed run, against the oracle's restatement of the reference's
+    DDP step (python/orca/distributed.py:238-256: f64 sum over ranks, x 1/W,
+    rounded to f32) computed on rank 0 for every rank's batch.
+    Step 1 from identical weights: every averaged gradient within 1e-5
+    (relative norm) of the oracle's; steps 2-3 run free: per-rank losses
+    within 1e-4, parameters within 1e-3 (a ReLU mask flip moves them ~3e-4),
+    and every rank's parameters bit-identical."""
+    import hashlib
+    import torch
+    from orcaml_b200.distributed import NcclCommunicator, nccl_unique_id
+    from orcaml_b200.mlp import MlpTrainer
+    dims, B, steps = [784, 1024, 1024, 10], 512, 3
+    kw = dict(lr=0.01, momentum=0.9)
+    t0 = time.perf_counter()
+    obj = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    comm = NcclCommunicator(be, rank, world, obj[0], timeout=120.0)
+    tr = MlpTrainer(be, dims, B, optimizer="sgd", gemm_path="tc", **kw)
+    tr.set_parameters(init_params(dims, 1))
+    tr.attach_comm(comm, bucket_bytes=64 << 20)
+    x, t, _ = make_batch(dims, B, rank)
+    losses, grads0 = [], None
+    for k in range(steps):
+        losses.append(tr.step(x, t))
+        if k == 0 and rank == 0:
+            grads0 = tr.get_grads()
+    params = tr.get_parameters()
+    digest = hashlib.sha256(b"".join(p.tobytes() for p in params)).hexdigest()
+    tr.attach_comm(None)
+    comm.close()
+    tr.close()
+    gathered = [None] * world
+    dist.all_gather_object(gathered, (losses, digest))
+    out = None
+    if rank == 0:
+        from oracle import oracle as O
+        O.set_threads(0)
+        O.set_gemm_threads(0)
+        ref = O.OracleTrainer(dims, init_params(dims, 1), optimizer="sgd", **kw)
+        batches = [make_batch(dims, B, r) for r in range(world)]
+        per = [O.mlp_forward_backward(dims, ref.params, bx, bt) for bx, bt, _ in batches]
+        avg = [O.ddp_average([p[1][i] for p in per]) for i in range(len(ref.params))]
+        g_err = max(float(np.linalg.norm(g.astype(np.float64) - r) /
+                          max(np.linalg.norm(r.astype(np.float64)), 1e-30))
+                    for g, r in zip(grads0, avg))
+        ref_losses = [[p[0] for p in per]]
+        ref.apply(avg)
+        for _ in range(steps - 1):
+            ref_losses.append(ref.step_ddp([b[0] for b in batches], [b[1] for b in batches]))
+        l_err = max(abs(gathered[r][0][k] - ref_losses[k][r]) / abs(ref_losses[k][r])
+                    for r in range(world) for k in range(steps))
+        p_err = max(float(np.linalg.norm(p.astype(np.float64) - q) /
+                          max(np.linalg.norm(q.astype(np.float64)), 1e-30))
+                    for p, q in zip(params, ref.params))
+        O.set_gemm_threads(1)
+        same = len({g[1] for g in gathered}) == 1
+        out = {"world": world, "model": "784-1024-1024-10, 512 rows per rank, SGD momentum 0.9, "
+                                        "3 steps, tensor-core path",
+               "grad_max_rel_err": g_err, "loss_max_rel_err": l_err,
+               "param_max_rel_err": p_err, "ranks_identical": same,
+               "ok": bool(same and g_err <= 1e-5 and l_err <= 1e-4 and p_err <= 1e-3),
+               "seconds": time.perf_counter() - t0}
+    torch.cuda.synchronize(local)
+    dist.barrier(device_ids=[local])
+    return out
 
 
 def run_ours(args):
@@ -223,6 +379,9 @@ def run_ours(args):
     from orcaml_b200.mlp import MlpTrainer
 
     be = CudaBackend(local)
+    parity = None
+    if world > 1 and not args.no_parity:
+        parity = ddp_parity_check(be, world, rank, dist, local)
     B = CFG.batch
     tr = MlpTrainer(be, CFG.dims, B, optimizer=CFG.optimizer, **opt_kwargs(CFG))
     tr.set_parameters(init_params(CFG.dims, 1))
@@ -271,27 +430,25 @@ def run_ours(args):
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     clocks.lines.clear()                       # keep only samples of the timed region
-    if True:
-        barrier()
-        ev0.record(stream)
-        if not use_graph:
-            tr.profile_begin()
-        for _ in range(args.steps):
-            device_step()
-        ev1.record(stream)
-        if not use_graph:
-            sites = tr.profile_end()
-        barrier()
-        clocks.__exit__(None, None, None)
+    barrier()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        device_step()
+    ev1.record(stream)
+    barrier()
+    clocks.__exit__(None, None, None)
     launches = be.launch_count() - launches0
+    # The per-kernel breakdown (and the roofline's GEMM time) comes from
+    # separate profiled steps after the timed ones, so the profiler's events
+    # stay out of `value`.
     if use_graph:
-        # The per-kernel breakdown comes from a few ordinary profiled steps
-        # (the replay is one launch, it cannot be split into sites).
         tr.graph_release()
-        tr.profile_begin()
-        for _ in range(3):
-            tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
-        sites = tr.profile_end()
+    prof_steps = max(3, min(args.steps, 10))
+    tr.profile_begin()
+    for _ in range(prof_steps):
+        tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+    sites = tr.profile_end()
+    barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_step = ms / args.steps
     value = world * B * args.steps / (ms / 1000.0)
@@ -354,8 +511,13 @@ def run_ours(args):
     if rank == 0:
         # configs[4]'s CPU step (1.4 B parameters, single-threaded GEMM) would
         # take hours even at 128 rows: not timed.
-        cpu = cpu_baseline(steps=1, batch=128) if (world == 1 and not args.no_cpu and
-                                                   CFG.name != "c4") else None
+        cpu = None
+        if world == 1 and not args.no_cpu and CFG.name != "c4":
+            big, small = sample_rows()
+            pts, cores = cpu_step_times([small, big])
+            cpu = cpu_baseline_from(pts, cores, f"one step at {small} rows and one at {big} rows of the "
+                                    f"{'-'.join(str(d) for d in CFG.dims)} {CFG.optimizer} step: "
+                                    f"GEMM one thread, element-wise loops on {cores} threads")
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
@@ -382,16 +544,20 @@ def run_ours(args):
                          "kernel": "tc_gemm_kernel (3xTF32 tcgen05, all GEMM launches of the step)",
                          "peak_note": f"{peak_src} bf16 dense {peaks['bf16_tflops']} TFLOP/s / 2 "
                                       "(tf32 rate) / 3 (products per FP32 product)",
-                         "launches_per_step": tc_launches / args.steps},
+                         "launches_per_step": tc_launches / prof_steps,
+                         "timing": f"CUDA events around each GEMM launch in {prof_steps} profiled "
+                                   "steps run after the timed ones"},
             "step_tflops": step_flops / (ms_step / 1e3) / 1e12,
             "gpu_launches": int(launches),
             "loss": loss_val,
             "breakdown_ms": breakdown,
+            "breakdown_note": f"per launch, from {prof_steps} profiled steps after the timed ones",
             "clocks": clocks.summary(),
         }
         if cpu is not None:
-            result["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
-            result["cpu_baseline"]["socket_ddp"] = socket_ddp_baseline()
+            result["cpu_baseline"] = dict(cpu, socket_ddp=socket_ddp_baseline())
+        if parity is not None:
+            result["ddp_parity"] = parity
         print(json.dumps(result), flush=True)
     if comm is not None:
         tr.attach_comm(None)
@@ -411,6 +577,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--bucket-mb", type=int, default=64)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the data-parallel parity pre-check (N > 1)")
     ap.add_argument("--e2e", default="staged", choices=["staged", "step"],
                     help="end-to-end leg: copies overlapped with the previous step, or not")
     ap.add_argument("--graph", action="store_true",

@@ -240,11 +240,10 @@ orca_status orca_softmax_ce_fwd_bwd(orca_ctx* ctx, const orca_buf* logits,
  * [batch, classes] (NULL for forward only).  The per-row scratch is a fixed
  * device array of 2^20 rows (4 MiB, resident on every GPU that loads the
  * library); larger batches are rejected with ORCA_INVALID_ARGUMENT.  The
- * first call on a device looks up that array's device address (a one-time
- * set-up, done with the device current); make this first call before any
- * stream capture.  All calls share the one array: calls that overlap on the
- * GPU (other streams, other host threads with their own contexts on the same
- * device) race on it. */
+ * array's device address is looked up once per device by orca_ctx_create
+ * (with that device current), so the call itself does no set-up.  All calls
+ * share the one array: calls that overlap on the GPU (other streams, other
+ * host threads with their own contexts on the same device) race on it. */
 orca_status orca_softmax_ce_fwd_bwd_noalloc(orca_ctx* ctx, const float* logits,
                                             const float* target, int64_t batch, int64_t classes,
                                             float* loss, float* dlogits);

@@ -85,6 +85,10 @@ def _declare(L):
                                 ctypes.c_int64]
     L.oc_ddp_average.argtypes = [PP, ctypes.c_int, ctypes.c_int64, _f32p]
     L.oc_set_gemm_order.argtypes = [ctypes.c_int]
+    L.oc_set_gemm_threads.argtypes = [ctypes.c_int]
+    L.oc_sgemm_packed.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int64,
+                                  ctypes.c_int64]
+    L.oc_sgemm_packed.restype = ctypes.c_int
     L.oc_set_threads.argtypes = [ctypes.c_int]
     L.oc_get_threads.restype = ctypes.c_int
 
@@ -108,8 +112,26 @@ def set_threads(n: int) -> None:
 
 
 def set_gemm_order(order: int) -> None:
-    """0: k ascending (default); 1: with FMA; 2: k-blocks of 256; 3: f64-rounded."""
+    """0: k ascending (default); 1: with FMA; 2: k-blocks of 256; 3: f64-rounded;
+    4: the packed FMA kernel (timing stand-in for the reference's matrixmultiply)."""
     lib().oc_set_gemm_order(int(order))
+
+
+def set_gemm_threads(n: int) -> None:
+    """Threads of the default-order GEMM (1 = single-threaded like the
+    reference; <= 0 = all).  Results are bit-identical at any count."""
+    lib().oc_set_gemm_threads(int(n))
+
+
+def sgemm_packed(a, b):
+    """C = A @ B with the timing stand-in GEMM (None without AVX2/FMA)."""
+    a, b = _f32(a), _f32(b)
+    m, k = a.shape
+    n = b.shape[1]
+    out = np.empty((m, n), np.float32)
+    if lib().oc_sgemm_packed(_p(a), _p(b), _p(out), m, k, n) != 0:
+        return None
+    return out
 
 
 def threads() -> int:

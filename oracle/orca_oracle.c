@@ -244,7 +244,9 @@ static void gemm_block(const float* A, const float* B, float* C, int64_t m,
  * how sensitive a training trajectory is to the (unpinned) summation order of
  * the reference's GEMM.  0: k ascending, separate multiply and add (default);
  * 1: k ascending with fused multiply-add; 2: partial sums over k-blocks of
- * 256, then added in block order; 3: exact product rounded once (f64). */
+ * 256, then added in block order; 3: exact product rounded once (f64);
+ * 4: the packed FMA kernel of sgemm_packed.c (timing stand-in for the
+ * reference's matrixmultiply; falls back to order 0 without AVX2/FMA). */
 static int g_gemm_order = 0;
 void oc_set_gemm_order(int order) { g_gemm_order = order; }
 
@@ -271,16 +273,48 @@ static void gemm_variant(const float* A, const float* B, float* C, int64_t m, in
     }
 }
 
+/* Threads of the default-order GEMM (1 = the reference's single thread).
+ * Rows are split between threads; every element keeps its k-ascending
+ * chain, so the result is the same bit for bit at any thread count.  Tests
+ * raise it to check wide layers in seconds; timed baselines keep 1. */
+static int g_gemm_threads = 1;
+void oc_set_gemm_threads(int n) { g_gemm_threads = n; }
+
+int oc_sgemm_packed(const float* A, const float* B, float* C, int64_t m, int64_t k, int64_t n);
+
+static void gemm_default(const float* A, const float* B, float* C, int64_t m, int64_t k,
+                         int64_t n) {
+  memset(C, 0, (size_t)(m * n) * sizeof(float));
+#ifdef _OPENMP
+  if (g_gemm_threads != 1 && m >= 16) {
+    const int nt = g_gemm_threads > 0 ? g_gemm_threads : omp_get_max_threads();
+    const int64_t rows = (m + nt - 1) / nt;
+#pragma omp parallel for num_threads(nt) schedule(static)
+    for (int t = 0; t < nt; ++t) {
+      const int64_t r0 = (int64_t)t * rows;
+      if (r0 < m) {
+        const int64_t rn = m - r0 < rows ? m - r0 : rows;
+        gemm_block(A + r0 * k, B, C + r0 * n, rn, k, n);
+      }
+    }
+    return;
+  }
+#endif
+  gemm_block(A, B, C, m, k, n);
+}
+
 void oc_matmul(const float* a, const float* b, float* c, int64_t batch,
                int64_t m, int64_t k, int64_t n) {
   for (int64_t bi = 0; bi < batch; ++bi) {
     float* cb = c + bi * m * n;
-    if (g_gemm_order != 0) {
-      gemm_variant(a + bi * m * k, b + bi * k * n, cb, m, k, n);
+    const float* ab = a + bi * m * k;
+    const float* bb = b + bi * k * n;
+    if (g_gemm_order == 4 && oc_sgemm_packed(ab, bb, cb, m, k, n) == 0) continue;
+    if (g_gemm_order != 0 && g_gemm_order != 4) {
+      gemm_variant(ab, bb, cb, m, k, n);
       continue;
     }
-    memset(cb, 0, (size_t)(m * n) * sizeof(float));
-    gemm_block(a + bi * m * k, b + bi * k * n, cb, m, k, n);
+    gemm_default(ab, bb, cb, m, k, n);
   }
 }
 

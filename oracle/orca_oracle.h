@@ -72,8 +72,15 @@ int oc_transpose(const float* in, const int64_t* shape, int rank,
 void oc_matmul(const float* a, const float* b, float* c,
                int64_t batch, int64_t m, int64_t k, int64_t n);
 /* Select an alternative FP32 summation order for oc_matmul (0 = default);
- * for sensitivity studies only. */
+ * for sensitivity studies only.  4 = the packed FMA kernel of
+ * sgemm_packed.c, a timing stand-in for matrixmultiply's design. */
 void oc_set_gemm_order(int order);
+/* Threads of the default-order GEMM (1, the reference's, by default; <= 0 =
+ * all).  Rows are split between threads, so results do not change. */
+void oc_set_gemm_threads(int n);
+/* Timing stand-in for matrixmultiply 0.3's sgemm (BLIS loop nest, packed
+ * panels, 8x8 FMA micro-kernel); -1 without AVX2/FMA. */
+int oc_sgemm_packed(const float* A, const float* B, float* C, int64_t m, int64_t k, int64_t n);
 
 /* ---- composed training step ------------------------------------------------ */
 /* Forward + softmax cross-entropy + backward of Sequential(Linear, ReLU, ...,

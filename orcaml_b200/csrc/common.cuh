@@ -23,6 +23,9 @@ namespace orca {
 // ---------------------------------------------------------------- host status
 void set_error(const char* fmt, ...);
 orca_status fail(orca_status s, const char* fmt, ...);
+// Looks up, once per device, the device address of the fixed scratch array of
+// orca_softmax_ce_fwd_bwd_noalloc (mlp.cu); the device must be current.
+orca_status ce_scratch_setup(int device);
 
 #define ORCA_CUDA_TRY(expr)                                                        \
   do {                                                                             \

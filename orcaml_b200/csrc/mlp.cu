@@ -84,6 +84,86 @@ __global__ void ce_kernel(const float* __restrict__ P, const float* __restrict__
   }
 }
 
+// The same computation with one warp per row, for wide rows (C > 32; the
+// thread-per-row form would read C-float rows strided across a warp and run
+// few threads, e.g. 2048 rows of C = 1000).  The row is staged in shared
+// memory with coalesced loads; every per-element term is computed by all
+// lanes in parallel, and each of the reference's serial sums runs on one
+// lane in ascending c over the staged terms, so the result is bit-identical
+// to ce_kernel.  Shared memory per warp: 5 * C floats.
+constexpr int CE_WIDE_MIN_C = 33, CE_WIDE_MAX_C = 8192;
+__global__ void ce_wide_kernel(const float* __restrict__ P, const float* __restrict__ T, int64_t B,
+                               int C, float inv_b, float* __restrict__ dP,
+                               float* __restrict__ row_loss) {
+  extern __shared__ float ce_sm[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t b = (int64_t)blockIdx.x * (blockDim.x / 32) + warp;
+  if (b >= B) return;   // whole warps leave together
+  float* sp = ce_sm + (size_t)warp * 5 * C;
+  float* st = sp + C;
+  float* se = st + C;
+  float* sq = se + C;
+  float* sr = sq + C;
+  const float* p = P + b * C;
+  const float* t = T + b * C;
+  float m = -3.402823466e38f;
+  for (int c = lane; c < C; c += 32) {
+    const float pv = p[c];
+    sp[c] = pv;
+    st[c] = t[c];
+    m = pv > m ? pv : m;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float q = __shfl_xor_sync(0xffffffffu, m, o);
+    m = q > m ? q : m;
+  }
+  for (int c = lane; c < C; c += 32) se[c] = expf(__fsub_rn(sp[c], m));
+  __syncwarp();
+  float s = 0.0f;
+  if (lane == 0)
+    for (int c = 0; c < C; ++c) s = __fadd_rn(s, se[c]);
+  s = __shfl_sync(0xffffffffu, s, 0);
+  const float lse = __fadd_rn(m, logf(fmaxf(s, 1e-7f)));
+  const float g_tl = __fmul_rn(inv_b, -1.0f);
+  for (int c = lane; c < C; c += 32) {
+    const float ls = __fsub_rn(sp[c], lse);
+    sq[c] = __fmul_rn(__fmul_rn(st[c], ls), -1.0f);
+    const float g_ls = __fadd_rn(0.0f, __fmul_rn(g_tl, st[c]));
+    const float g_lse = __fadd_rn(0.0f, __fmul_rn(g_ls, -1.0f));
+    sr[c] = __fdiv_rn(__fadd_rn(0.0f, g_lse), s);
+  }
+  __syncwarp();
+  // Lane 0: the loss sum; lane 1: g_s0 -- the same loop over different arrays.
+  float acc = 0.0f;
+  if (lane < 2) {
+    const float* arr = lane == 0 ? sq : sr;
+    for (int c = 0; c < C; ++c) acc = __fadd_rn(acc, arr[c]);
+  }
+  const float per = __shfl_sync(0xffffffffu, acc, 0);
+  const float g_s0 = __shfl_sync(0xffffffffu, acc, 1);
+  if (lane == 0) row_loss[b] = per;
+  if (!dP) return;
+  __syncwarp();
+  for (int c = lane; c < C; c += 32) {
+    const float g_ls = __fadd_rn(0.0f, __fmul_rn(g_tl, st[c]));
+    const float g_lse = __fadd_rn(0.0f, __fmul_rn(g_ls, -1.0f));
+    const float g_s = __fmul_rn(g_s0, se[c]);
+    sq[c] = __fadd_rn(__fadd_rn(0.0f, g_lse), __fadd_rn(0.0f, __fmul_rn(g_s, -1.0f)));
+    sr[c] = __fadd_rn(__fadd_rn(0.0f, g_ls), __fadd_rn(0.0f, g_s));
+  }
+  __syncwarp();
+  float g_m0 = 0.0f;
+  if (lane == 0)
+    for (int c = 0; c < C; ++c) g_m0 = __fadd_rn(g_m0, sq[c]);
+  g_m0 = __shfl_sync(0xffffffffu, g_m0, 0);
+  float* d = dP + b * C;
+  for (int c = lane; c < C; c += 32) {
+    const float gi = sp[c] == m ? __fadd_rn(0.0f, g_m0) : 0.0f;
+    d[c] = __fadd_rn(sr[c], gi);
+  }
+}
+
 // loss = (sum_b row_loss[b]) * (1/B); a fixed-shape tree, so deterministic.
 __global__ void ce_loss_kernel(const float* __restrict__ row_loss, int64_t B, float inv_b,
                                float* __restrict__ loss) {
@@ -124,6 +204,28 @@ __global__ void colsum_final_kernel(const float* __restrict__ part, int chunks, 
   float acc = 0.0f;
   for (int c = 0; c < chunks; ++c) acc = __fadd_rn(acc, part[(int64_t)c * N + n]);
   out[n] = acc;
+}
+
+// Row losses of a softmax-CE batch (ce_kernel or, for wide rows, ce_wide_kernel).
+static void launch_ce_rows(cudaStream_t stream, const float* P, const float* T, int64_t B,
+                           int64_t C, float inv_b, float* dP, float* rows) {
+  if (C >= CE_WIDE_MIN_C && C <= CE_WIDE_MAX_C) {
+    // Warps per block so that 5*C floats per warp stay within 96 KB a block
+    // (one warp of 160 KB at the widest rows).
+    const int wpb = (int)std::max<int64_t>(1, std::min<int64_t>(8, (96 * 1024) / (20 * C)));
+    const size_t smem = (size_t)wpb * 20 * (size_t)C;
+    static std::once_flag attr_once[128];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::call_once(attr_once[dev & 127], [] {
+      cudaFuncSetAttribute(ce_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           20 * CE_WIDE_MAX_C);
+    });
+    ce_wide_kernel<<<(unsigned)cdiv(B, wpb), 32 * wpb, smem, stream>>>(P, T, B, (int)C, inv_b, dP,
+                                                                     rows);
+  } else {
+    ce_kernel<<<(unsigned)cdiv(B, 128), 128, 0, stream>>>(P, T, B, C, inv_b, dP, rows);
+  }
 }
 
 struct SgdArgs {
@@ -1071,9 +1173,8 @@ orca_status orca_mlp_forward(orca_mlp* m, const float* x, const float* t, float*
   }
   ORCA_TRY(mlp_forward_impl(m, false));
   if (t) {
-    ce_kernel<<<(unsigned)cdiv(B, 128), 128, 0, ctx->stream>>>(m->logits, m->t_buf, B, C,
-                                                              1.0f / (float)B, nullptr,
-                                                              m->row_loss);
+    launch_ce_rows(ctx->stream, m->logits, m->t_buf, B, C, 1.0f / (float)B, nullptr,
+                   m->row_loss);
     ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(m->row_loss, B, 1.0f / (float)B, m->loss);
     count_launch(ctx, 2);
   }
@@ -1193,9 +1294,8 @@ static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad) {
   }
   if (with_loss_grad) {
     const int pr = prof_open(m, "softmax_ce", 0.0, 4.0 * (3 * B * C + B));
-    ce_kernel<<<(unsigned)cdiv(B, 128), 128, 0, ctx->stream>>>(m->logits, m->t_buf, B, C,
-                                                              1.0f / (float)B, m->dlogits,
-                                                              m->row_loss);
+    launch_ce_rows(ctx->stream, m->logits, m->t_buf, B, C, 1.0f / (float)B, m->dlogits,
+                   m->row_loss);
     ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(m->row_loss, B, 1.0f / (float)B, m->loss);
     count_launch(ctx, 2);
     prof_close(m, pr);
@@ -1539,8 +1639,8 @@ orca_status orca_softmax_ce_fwd_bwd(orca_ctx* ctx, const orca_buf* logits, const
   float* rows = nullptr;
   ORCA_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&rows), (size_t)batch * 4, ctx->stream));
   const float inv_b = 1.0f / (float)batch;
-  ce_kernel<<<(unsigned)cdiv(batch, 128), 128, 0, ctx->stream>>>(
-      (const float*)logits->ptr, (const float*)target->ptr, batch, classes, inv_b, dp, rows);
+  launch_ce_rows(ctx->stream, (const float*)logits->ptr, (const float*)target->ptr, batch,
+                 classes, inv_b, dp, rows);
   ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(rows, batch, inv_b, (float*)(*loss)->ptr);
   count_launch(ctx, 2);
   cudaFreeAsync(rows, ctx->stream);
@@ -1553,28 +1653,32 @@ orca_status orca_softmax_ce_fwd_bwd(orca_ctx* ctx, const orca_buf* logits, const
 // array instead of a per-call allocation.  Every GPU that loads the library
 // holds it until the process exits.  Host code must not hand the symbol
 // itself to a kernel (on the host it is only a stand-in for the device
-// array); the device address is looked up once per device below.
+// array); its device address is looked up once per device when a context is
+// created on that device (orca_ctx_create, device current), so the entry
+// point itself makes no runtime look-up.
 }  // extern "C"
 
 namespace orca {
 constexpr int64_t kCeScratchRows = int64_t(1) << 20;   // 4 MiB of f32 row losses
 static __device__ __align__(256) float g_ce_row_scratch[kCeScratchRows];
-static float* g_ce_scratch_addr[128] = {};              // per device, set once
+constexpr int kMaxDevices = 128;
+static std::atomic<float*> g_ce_scratch_addr[kMaxDevices] = {};   // per device, set once
 static std::mutex g_ce_scratch_mu;
 
-static orca_status ce_scratch_for(int device, float** out) {
-  if (device < 0 || device >= 128) return fail(ORCA_INVALID_ARGUMENT, "device index %d", device);
+// Called by orca_ctx_create with `device` current.  Idempotent.
+orca_status ce_scratch_setup(int device) {
+  if (device < 0 || device >= kMaxDevices)
+    return fail(ORCA_INVALID_ARGUMENT, "device index %d", device);
   std::lock_guard<std::mutex> lk(g_ce_scratch_mu);
-  if (!g_ce_scratch_addr[device]) {
-    // The device must be current here (the caller has made it so).
-    void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_ce_row_scratch);
-    if (e != cudaSuccess || !ptr)
-      return fail(ORCA_CUDA_ERROR, "cudaGetSymbolAddress(row-loss scratch) failed: %s",
-                  cudaGetErrorString(e));
-    g_ce_scratch_addr[device] = static_cast<float*>(ptr);
+  if (g_ce_scratch_addr[device].load()) return ORCA_OK;
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_ce_row_scratch);
+  if (e != cudaSuccess || !ptr) {
+    (void)cudaGetLastError();   // not sticky: keep it from failing a later, unrelated check
+    return fail(ORCA_CUDA_ERROR, "cudaGetSymbolAddress(row-loss scratch) failed: %s",
+                cudaGetErrorString(e));
   }
-  *out = g_ce_scratch_addr[device];
+  g_ce_scratch_addr[device].store(static_cast<float*>(ptr));
   return ORCA_OK;
 }
 }  // namespace orca
@@ -1593,13 +1697,14 @@ orca_status orca_softmax_ce_fwd_bwd_noalloc(orca_ctx* ctx, const float* logits,
                 "batch %lld exceeds the %lld rows of the fixed no-allocation scratch; "
                 "use orca_softmax_ce_fwd_bwd for larger batches",
                 (long long)batch, (long long)kCeScratchRows);
-  float* rows = nullptr;
-  ORCA_TRY(ce_scratch_for(ctx->device, &rows));
+  float* rows = ctx->device < kMaxDevices ? g_ce_scratch_addr[ctx->device].load() : nullptr;
+  if (!rows)
+    return fail(ORCA_INTERNAL, "the no-allocation scratch of device %d was not set up when "
+                "its context was created", ctx->device);
   // Every row of the scratch that ce_loss_kernel reads is written first by
   // ce_kernel on the same stream, so nothing needs clearing between calls.
   const float inv_b = 1.0f / (float)batch;
-  ce_kernel<<<(unsigned)cdiv(batch, 128), 128, 0, ctx->stream>>>(logits, target, batch, classes,
-                                                                inv_b, dlogits, rows);
+  launch_ce_rows(ctx->stream, logits, target, batch, classes, inv_b, dlogits, rows);
   ce_loss_kernel<<<1, 1024, 0, ctx->stream>>>(rows, batch, inv_b, loss);
   count_launch(ctx, 2);
   ORCA_CUDA_TRY(cudaGetLastError());

@@ -414,6 +414,10 @@ orca_status orca_ctx_create(int device, orca_ctx** out) {
   ORCA_CUDA_TRY(cudaMemset(c->dev_err, 0, sizeof(int)));
   ORCA_CUDA_TRY(cudaMalloc(&c->tile_ctr, sizeof(int)));
   ORCA_CUDA_TRY(cudaMemset(c->tile_ctr, 0, sizeof(int)));
+  // Device address of the no-allocation CE entry point's fixed scratch,
+  // looked up now with the device current (allocates nothing).  A failure
+  // here only disables that entry point, which then reports it.
+  if (ce_scratch_setup(device) != ORCA_OK) set_error("");
   // Keep freed stream-ordered allocations in the pool instead of returning
   // them to the driver at every synchronisation.
   cudaMemPool_t pool;

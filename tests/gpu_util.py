@@ -24,3 +24,47 @@ def rel_err(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def f64_forward_backward(dims, params, x, t):
+    """The step's exact values: forward, softmax cross-entropy (mean over the
+    batch) and backward of Sequential(Linear, ReLU, ..., Linear) in float64,
+    from the same float32 inputs and parameters.  Gradients come back in
+    Module.parameters() order (W0, b0, W1, b1, ...), with the ReLU masks taken
+    from the pre-activation as the reference's ReluBackward does
+    (orca-autograd/src/backend.rs:1624-1646).  Returns (loss, grads, logits)."""
+    L = len(dims) - 1
+    acts = [np.asarray(x, np.float64)]
+    pre = []
+    Ws = [np.asarray(params[2 * l], np.float64) for l in range(L)]
+    for l in range(L):
+        z = acts[-1] @ Ws[l] + np.asarray(params[2 * l + 1], np.float64)
+        pre.append(z)
+        if l + 1 < L:
+            acts.append(np.maximum(z, 0.0))
+    P = pre[-1]
+    T = np.asarray(t, np.float64)
+    B = P.shape[0]
+    m = P.max(axis=1, keepdims=True)
+    e = np.exp(P - m)
+    s = e.sum(axis=1, keepdims=True)
+    loss = float(-(T * (P - m - np.log(s))).sum() / B)
+    g = (e / s * T.sum(axis=1, keepdims=True) - T) / B
+    grads = [None] * (2 * L)
+    for l in range(L - 1, -1, -1):
+        grads[2 * l] = acts[l].T @ g
+        grads[2 * l + 1] = g.sum(axis=0, keepdims=True)
+        if l > 0:
+            g = (g @ Ws[l].T) * (pre[l - 1] > 0.0)
+    return loss, grads, P
+
+
+def argmax_agrees(logits, ref_logits, margin=1e-5):
+    """Argmax of every row equal, except rows whose two largest reference
+    logits are within margin * max|logit| of each other (a near-tie that any
+    correct FP32 order may break either way).  Returns the rows compared."""
+    ref = np.asarray(ref_logits, np.float64)
+    top2 = np.sort(ref, axis=1)[:, -2:]
+    clear = (top2[:, 1] - top2[:, 0]) > margin * np.abs(ref).max()
+    assert np.array_equal(np.argmax(logits, axis=1)[clear], np.argmax(ref, axis=1)[clear])
+    return int(clear.sum())

@@ -165,6 +165,23 @@ def test_softmax_ce_large_batch(be):
     np.testing.assert_allclose(be.to_f32_vec(dp_s).reshape(4096, 10), ref_dp, rtol=1e-5, atol=1e-9)
 
 
+@pytest.mark.parametrize("B,C", [(2048, 1000), (3, 33), (37, 100), (5, 4099), (9, 8192)])
+def test_softmax_ce_wide_rows_match_oracle(be, B, C):
+    """Rows wider than 32 classes take the warp-per-row kernel (configs[4]'s
+    C = 1000 among them): the same serial sums as the reference, so the loss
+    and dP agree with the oracle up to expf/logf's ulps; rows with tied
+    maxima exercise MaxToShapeBackward's tie rule."""
+    P = (RNG.standard_normal((B, C)) * 3).astype(np.float32)
+    P[0, : min(C, 4)] = P[0].max() + 1.0          # a four-way tie at the maximum
+    T = np.zeros((B, C), np.float32)
+    T[np.arange(B), RNG.integers(0, C, B)] = 1.0
+    T[-1] = 1.0 / C                                # a soft target row
+    loss_s, dp_s = be.softmax_ce_fwd_bwd(up(be, P), up(be, T), B, C)
+    ref_loss, ref_dp = O.softmax_ce(P, T)
+    assert abs(be.to_f32_vec(loss_s)[0] - ref_loss) <= 1e-5 * abs(ref_loss)
+    np.testing.assert_allclose(down(be, dp_s, (B, C)), ref_dp, rtol=1e-5, atol=1e-9)
+
+
 @pytest.mark.parametrize("opt", ["sgd", "sgdm", "sgdm_wd_damp", "adamw"])
 def test_optimizer_kernels_bit_exact(be, opt):
     n = 10007
