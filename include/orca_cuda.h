@@ -285,6 +285,11 @@ orca_status orca_mlp_set_param(orca_mlp* mlp, int index, const float* host, int6
 orca_status orca_mlp_get_param(orca_mlp* mlp, int index, float* host, int64_t numel);
 /* Gradient of the last backward (after the all-reduce when a comm is attached). */
 orca_status orca_mlp_get_grad(orca_mlp* mlp, int index, float* host, int64_t numel);
+/* Inspection (no counterpart in the reference, which keeps activations in
+ * its tape): the input of Linear `layer` (1..n_layers-1) in the last forward,
+ * i.e. the ReLU output of the layer below, [batch, dims[layer]].  Parity
+ * tests read the ReLU masks the step used from it. */
+orca_status orca_mlp_get_activation(orca_mlp* mlp, int layer, float* host, int64_t numel);
 /* Optimizer state of parameter `index` for checkpoints (the reference's
  * optimizers keep it in Python objects and never save it, optim/sgd.py:46-79,
  * adamw.py:48-99): slot 0 = SGD velocity / AdamW first moment m, slot 1 =
@@ -299,6 +304,18 @@ orca_status orca_mlp_get_step(const orca_mlp* mlp, int64_t* t, int* velocity_sta
 orca_status orca_mlp_set_step(orca_mlp* mlp, int64_t t, int velocity_started);
 /* Attach (or detach with NULL) the communicator used by every later step. */
 orca_status orca_mlp_attach_comm(orca_mlp* mlp, orca_comm* comm, size_t bucket_bytes);
+/* The gradient exchange plan a runner with these dims and bucket size uses
+ * (host only; no device needed), replacing the per-parameter loop of
+ * DistributedDataParallel.all_reduce_gradients (python/orca/distributed.py:
+ * 222-256).  The gradient arena holds the parameters in Module.parameters()
+ * order (python/orca/nn/module.py:32-44); bucket i covers floats
+ * [offsets[i], offsets[i] + counts[i]) of it and belongs to layer layers[i].
+ * Buckets come in exchange order: last layer first, each layer's (dW, db)
+ * range in pieces of at most bucket_bytes (0 = whole layer).  With all three
+ * arrays NULL only *n_buckets is set. */
+orca_status orca_mlp_bucket_plan(int n_layers, const int64_t* dims, size_t bucket_bytes,
+                                 int capacity, int64_t* offsets, int64_t* counts, int* layers,
+                                 int* n_buckets);
 /* One training step with host inputs: x [batch, dims[0]] and the one-hot (or
  * soft) target t [batch, dims[n_layers]] are copied to the device inside the
  * call; *loss (host, nullable) receives this rank's loss (read back). */

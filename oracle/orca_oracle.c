@@ -280,7 +280,8 @@ static void gemm_variant(const float* A, const float* B, float* C, int64_t m, in
 static int g_gemm_threads = 1;
 void oc_set_gemm_threads(int n) { g_gemm_threads = n; }
 
-int oc_sgemm_packed(const float* A, const float* B, float* C, int64_t m, int64_t k, int64_t n);
+int oc_sgemm_packed_mt(const float* A, const float* B, float* C, int64_t m, int64_t k, int64_t n,
+                       int threads);
 
 static void gemm_default(const float* A, const float* B, float* C, int64_t m, int64_t k,
                          int64_t n) {
@@ -309,7 +310,14 @@ void oc_matmul(const float* a, const float* b, float* c, int64_t batch,
     float* cb = c + bi * m * n;
     const float* ab = a + bi * m * k;
     const float* bb = b + bi * k * n;
-    if (g_gemm_order == 4 && oc_sgemm_packed(ab, bb, cb, m, k, n) == 0) continue;
+    if (g_gemm_order == 4) {
+#ifdef _OPENMP
+      const int nt = g_gemm_threads > 0 ? g_gemm_threads : omp_get_max_threads();
+#else
+      const int nt = 1;
+#endif
+      if (oc_sgemm_packed_mt(ab, bb, cb, m, k, n, nt) == 0) continue;
+    }
     if (g_gemm_order != 0 && g_gemm_order != 4) {
       gemm_variant(ab, bb, cb, m, k, n);
       continue;

@@ -86,50 +86,72 @@ static void pack_b(const float* B, int64_t ldb, int64_t kc, int64_t nc, float* o
   }
 }
 
-/* C (m x n, row-major) = A (m x k) * B (k x n).  Returns -1 when the CPU
- * lacks AVX2/FMA or memory runs out (the caller then uses its own loop). */
-int oc_sgemm_packed(const float* A, const float* B, float* C, int64_t m, int64_t k, int64_t n) {
+/* Row blocks of MC rows of one (column block, depth block) step.  Every
+ * element of C belongs to exactly one row block, so splitting row blocks
+ * between threads leaves each element's arithmetic unchanged. */
+static void row_blocks(const float* A, float* C, int64_t m, int64_t k, int64_t n, int64_t j0,
+                       int64_t nc, int64_t p0, int64_t kc, const float* bpack, int64_t i_first,
+                       int64_t i_step, float* apack) {
+  float tmp[MR * NR];
+  for (int64_t i0 = i_first; i0 < m; i0 += i_step) {
+    const int64_t mc = m - i0 < MC ? m - i0 : MC;
+    pack_a(A + i0 * k + p0, k, mc, kc, apack);
+    for (int64_t jr = 0; jr < nc; jr += NR) {
+      const int64_t nr = nc - jr < NR ? nc - jr : NR;
+      for (int64_t ir = 0; ir < mc; ir += MR) {
+        const int64_t mr = mc - ir < MR ? mc - ir : MR;
+        float* c = C + (i0 + ir) * n + j0 + jr;
+        const float* ap = apack + ir * kc;
+        const float* bp = bpack + jr * kc;
+        if (mr == MR && nr == NR) {
+          kernel_8x8(kc, ap, bp, c, n, p0 > 0);
+        } else {
+          kernel_8x8(kc, ap, bp, tmp, NR, 0);
+          for (int64_t i = 0; i < mr; ++i)
+            for (int64_t j = 0; j < nr; ++j)
+              c[i * n + j] = p0 > 0 ? c[i * n + j] + tmp[i * NR + j] : tmp[i * NR + j];
+        }
+      }
+    }
+  }
+}
+
+/* C (m x n, row-major) = A (m x k) * B (k x n) on `threads` threads (1 = the
+ * reference's single thread; the result does not depend on it).  Returns -1
+ * when the CPU lacks AVX2/FMA or memory runs out (the caller then uses its
+ * own loop). */
+int oc_sgemm_packed_mt(const float* A, const float* B, float* C, int64_t m, int64_t k, int64_t n,
+                       int threads) {
   if (!__builtin_cpu_supports("avx2") || !__builtin_cpu_supports("fma")) return -1;
+  if (threads < 1) threads = 1;
   float* bpack = (float*)aligned_alloc(64, sizeof(float) * KC * (NC + NR));
-  float* apack = (float*)aligned_alloc(64, sizeof(float) * KC * (MC + MR));
+  float* apack = (float*)aligned_alloc(64, sizeof(float) * KC * (MC + MR) * (size_t)threads);
   if (!bpack || !apack) {
     free(bpack);
     free(apack);
     return -1;
   }
-  float tmp[MR * NR];
-  if (k == 0) {
-    memset(C, 0, sizeof(float) * (size_t)(m * n));
-  }
+  if (k == 0) memset(C, 0, sizeof(float) * (size_t)(m * n));
   for (int64_t j0 = 0; j0 < n; j0 += NC) {
     const int64_t nc = n - j0 < NC ? n - j0 : NC;
     for (int64_t p0 = 0; p0 < k; p0 += KC) {
       const int64_t kc = k - p0 < KC ? k - p0 : KC;
       pack_b(B + p0 * n + j0, n, kc, nc, bpack);
-      for (int64_t i0 = 0; i0 < m; i0 += MC) {
-        const int64_t mc = m - i0 < MC ? m - i0 : MC;
-        pack_a(A + i0 * k + p0, k, mc, kc, apack);
-        for (int64_t jr = 0; jr < nc; jr += NR) {
-          const int64_t nr = nc - jr < NR ? nc - jr : NR;
-          for (int64_t ir = 0; ir < mc; ir += MR) {
-            const int64_t mr = mc - ir < MR ? mc - ir : MR;
-            float* c = C + (i0 + ir) * n + j0 + jr;
-            const float* ap = apack + ir * kc;
-            const float* bp = bpack + jr * kc;
-            if (mr == MR && nr == NR) {
-              kernel_8x8(kc, ap, bp, c, n, p0 > 0);
-            } else {
-              kernel_8x8(kc, ap, bp, tmp, NR, 0);
-              for (int64_t i = 0; i < mr; ++i)
-                for (int64_t j = 0; j < nr; ++j)
-                  c[i * n + j] = p0 > 0 ? c[i * n + j] + tmp[i * NR + j] : tmp[i * NR + j];
-            }
-          }
-        }
+      if (threads == 1) {
+        row_blocks(A, C, m, k, n, j0, nc, p0, kc, bpack, 0, MC, apack);
+      } else {
+#pragma omp parallel for num_threads(threads) schedule(static, 1)
+        for (int t = 0; t < threads; ++t)
+          row_blocks(A, C, m, k, n, j0, nc, p0, kc, bpack, (int64_t)t * MC,
+                     (int64_t)threads * MC, apack + (size_t)t * KC * (MC + MR));
       }
     }
   }
   free(bpack);
   free(apack);
   return 0;
+}
+
+int oc_sgemm_packed(const float* A, const float* B, float* C, int64_t m, int64_t k, int64_t n) {
+  return oc_sgemm_packed_mt(A, B, C, m, k, n, 1);
 }

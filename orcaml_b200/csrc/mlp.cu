@@ -503,6 +503,32 @@ orca_status colsum(orca_ctx* ctx, const float* hi, const float* lo, int64_t B, i
 
 using namespace orca;
 
+// The gradient exchange plan.  The arena holds the gradients in
+// Module.parameters() order (python/orca/nn/module.py:32-44: W0, b0, W1, b1,
+// ...), so each layer's (dW, db) is one contiguous range; the layers are
+// exchanged last layer first (the order the backward pass finishes them in),
+// each in buckets of at most bucket_bytes (0: the whole layer).  The
+// reference averages every parameter independently
+// (python/orca/distributed.py:238-256), so neither the order nor the bucket
+// boundaries change any result.
+struct Bucket {
+  int64_t offset, count;
+  int layer;
+};
+static void bucket_plan(int L, const int64_t* dims, size_t bucket_bytes, std::vector<Bucket>& out) {
+  std::vector<int64_t> layer_off(L);
+  int64_t off = 0;
+  for (int l = 0; l < L; ++l) {
+    layer_off[l] = off;
+    off += dims[l] * dims[l + 1] + dims[l + 1];
+  }
+  for (int l = L - 1; l >= 0; --l) {
+    const int64_t n = dims[l] * dims[l + 1] + dims[l + 1];
+    const int64_t chunk = bucket_bytes ? std::max<int64_t>((int64_t)(bucket_bytes / 4), 1) : n;
+    for (int64_t o = 0; o < n; o += chunk) out.push_back({layer_off[l] + o, std::min(chunk, n - o), l});
+  }
+}
+
 // =============================================================== step runner
 struct orca_mlp {
   orca_ctx* ctx = nullptr;
@@ -881,6 +907,28 @@ orca_status orca_mlp_get_param(orca_mlp* m, int index, float* host, int64_t nume
   return check_device_error(m->ctx);
 }
 
+orca_status orca_mlp_get_activation(orca_mlp* m, int layer, float* host, int64_t numel) {
+  if (!m || !host) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (layer < 1 || layer >= m->L)
+    return fail(ORCA_INVALID_ARGUMENT, "layer %d: hidden activations are layers 1..%d", layer,
+                m->L - 1);
+  const int64_t n = m->B * m->dims[layer];
+  if (numel != n)
+    return fail(ORCA_SHAPE_MISMATCH, "get_activation: %lld elements expected", (long long)n);
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  float* tmp = nullptr;
+  ORCA_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&tmp), (size_t)n * 4, m->ctx->stream));
+  merge_planes_kernel<<<ew_grid(m->ctx, n), 256, 0, m->ctx->stream>>>(
+      m->act_planes[layer], m->act_planes[layer] + n, tmp, n);
+  count_launch(m->ctx);
+  orca_status st = finish_sync(m);
+  if (st == ORCA_OK) st = copy_to_host(m->ctx, host, tmp, (size_t)n * 4);
+  cudaFreeAsync(tmp, m->ctx->stream);
+  ORCA_TRY(st);
+  return check_device_error(m->ctx);
+}
+
 orca_status orca_mlp_get_grad(orca_mlp* m, int index, float* host, int64_t numel) {
   int64_t n;
   ORCA_TRY(orca_mlp_param_numel(m, index, &n));
@@ -939,6 +987,27 @@ orca_status orca_mlp_set_step(orca_mlp* m, int64_t t, int velocity_started) {
   std::lock_guard<std::mutex> lk(m->ctx->mu);
   m->t = t;
   m->vel_init = velocity_started != 0;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_bucket_plan(int n_layers, const int64_t* dims, size_t bucket_bytes,
+                                 int capacity, int64_t* offsets, int64_t* counts, int* layers,
+                                 int* n_buckets) {
+  if (!dims || !n_buckets) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  if (n_layers < 1 || n_layers > 60) return fail(ORCA_INVALID_ARGUMENT, "n_layers");
+  for (int i = 0; i <= n_layers; ++i)
+    if (dims[i] < 1) return fail(ORCA_INVALID_ARGUMENT, "dims must be positive");
+  std::vector<Bucket> plan;
+  bucket_plan(n_layers, dims, bucket_bytes, plan);
+  *n_buckets = (int)plan.size();
+  if (!offsets && !counts && !layers) return ORCA_OK;
+  if (capacity < (int)plan.size())
+    return fail(ORCA_INVALID_ARGUMENT, "capacity %d < %d buckets", capacity, (int)plan.size());
+  for (size_t i = 0; i < plan.size(); ++i) {
+    if (offsets) offsets[i] = plan[i].offset;
+    if (counts) counts[i] = plan[i].count;
+    if (layers) layers[i] = plan[i].layer;
+  }
   return ORCA_OK;
 }
 
@@ -1331,17 +1400,17 @@ static orca_status launch_layer_allreduce(orca_mlp* m, int l) {
   orca_ctx* ctx = m->ctx;
   ORCA_CUDA_TRY(cudaEventRecord(m->ev_layer[l], ctx->stream));
   ORCA_CUDA_TRY(cudaStreamWaitEvent(ctx->comm_stream, m->ev_layer[l], 0));
-  // The layer's (dW, db) are contiguous in the arena.
-  float* base = m->grads + m->p_off[2 * l];
-  size_t n = (size_t)(m->dims[l] * m->dims[l + 1] + m->dims[l + 1]);
+  std::vector<Bucket> plan;
+  bucket_plan(m->L, m->dims.data(), m->bucket_bytes, plan);
   // Timed on the comm stream: from the layer's gradients being ready to
   // their average being complete (includes waiting for SMs).
+  const int64_t n = m->dims[l] * m->dims[l + 1] + m->dims[l + 1];
   const int pr = prof_open(m, "allreduce_l" + std::to_string(l), 0.0, 4.0 * (double)n, -1,
                            ctx->comm_stream);
-  size_t chunk = m->bucket_bytes ? std::max<size_t>(m->bucket_bytes / 4, 1) : n;
-  for (size_t off = 0; off < n; off += chunk) {
-    size_t c = std::min(chunk, n - off);
-    ORCA_TRY(comm_allreduce_avg_stream(m->comm, base + off, c, ctx->comm_stream));
+  for (const Bucket& b : plan) {
+    if (b.layer != l) continue;
+    ORCA_TRY(comm_allreduce_avg_stream(m->comm, m->grads + b.offset, (size_t)b.count,
+                                       ctx->comm_stream));
   }
   prof_close(m, pr);
   ORCA_CUDA_TRY(cudaEventRecord(m->ev_reduced[l], ctx->comm_stream));

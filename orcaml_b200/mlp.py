@@ -135,6 +135,14 @@ class MlpTrainer:
             out.append(a)
         return out
 
+    def get_activation(self, layer: int) -> np.ndarray:
+        """Input of Linear `layer` (1..n_layers-1) in the last forward: the
+        ReLU output of the layer below, [batch, dims[layer]]."""
+        a = np.empty((self.batch, self.dims[layer]), dtype=np.float32)
+        L.check(L.load().orca_mlp_get_activation(self._h, int(layer),
+                                                 a.ctypes.data_as(ctypes.c_void_p), a.size))
+        return a
+
     # -- checkpoints (safetensors)
     def param_names(self) -> List[str]:
         """The keys the reference's Module.save_weights gives the same model

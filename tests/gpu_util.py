@@ -26,23 +26,36 @@ def rel_err(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def f64_forward_backward(dims, params, x, t):
+def f64_forward_backward(dims, params, x, t, masks=None):
     """The step's exact values: forward, softmax cross-entropy (mean over the
     batch) and backward of Sequential(Linear, ReLU, ..., Linear) in float64,
     from the same float32 inputs and parameters.  Gradients come back in
     Module.parameters() order (W0, b0, W1, b1, ...), with the ReLU masks taken
     from the pre-activation as the reference's ReluBackward does
-    (orca-autograd/src/backend.rs:1624-1646).  Returns (loss, grads, logits)."""
+    (orca-autograd/src/backend.rs:1624-1646).
+
+    masks (optional): one boolean array per hidden layer, the ReLU pattern to
+    use instead of the float64 sign of each pre-activation -- the pattern an
+    FP32 step actually used.  A pre-activation within rounding distance of
+    zero can take either sign under any correct FP32 summation order (the
+    reference's included); with the FP32 step's own pattern the remaining
+    difference is the arithmetic alone.
+
+    Returns (loss, grads, logits, pre) with pre the float64 pre-activations
+    of the hidden layers."""
     L = len(dims) - 1
     acts = [np.asarray(x, np.float64)]
-    pre = []
+    pre, used = [], []
     Ws = [np.asarray(params[2 * l], np.float64) for l in range(L)]
     for l in range(L):
         z = acts[-1] @ Ws[l] + np.asarray(params[2 * l + 1], np.float64)
-        pre.append(z)
         if l + 1 < L:
-            acts.append(np.maximum(z, 0.0))
-    P = pre[-1]
+            pre.append(z)
+            mask = (z > 0.0) if masks is None else np.asarray(masks[l], bool)
+            used.append(mask)
+            acts.append(np.where(mask, z, 0.0))
+        else:
+            P = z
     T = np.asarray(t, np.float64)
     B = P.shape[0]
     m = P.max(axis=1, keepdims=True)
@@ -55,8 +68,32 @@ def f64_forward_backward(dims, params, x, t):
         grads[2 * l] = acts[l].T @ g
         grads[2 * l + 1] = g.sum(axis=0, keepdims=True)
         if l > 0:
-            g = (g @ Ws[l].T) * (pre[l - 1] > 0.0)
-    return loss, grads, P
+            g = (g @ Ws[l].T) * used[l - 1]
+    return loss, grads, P, pre
+
+
+def gpu_masks(trainer):
+    """The ReLU pattern of each hidden layer in the trainer's last forward."""
+    return [trainer.get_activation(l) > 0.0 for l in range(1, len(trainer.dims) - 1)]
+
+
+def check_mask_flips(masks, pre, x, params, tol=1e-5):
+    """Every hidden unit whose FP32 ReLU decision differs from the exact sign
+    of its pre-activation must be a near-tie: |z| <= tol * (|a| @ |W| + |b|),
+    the accumulated magnitude of the terms summed into z.  Returns the number
+    of such flips."""
+    flips = 0
+    a = np.abs(np.asarray(x, np.float64))
+    for l, (mask, z) in enumerate(zip(masks, pre)):
+        scale = a @ np.abs(np.asarray(params[2 * l], np.float64)) + \
+            np.abs(np.asarray(params[2 * l + 1], np.float64))
+        diff = mask != (z > 0.0)
+        flips += int(diff.sum())
+        if diff.any():
+            worst = float(np.max(np.abs(z[diff]) / scale[diff]))
+            assert worst <= tol, f"layer {l}: a ReLU decision differs at |z| = {worst:.3g} x scale"
+        a = np.where(mask, np.abs(z), 0.0)
+    return flips
 
 
 def argmax_agrees(logits, ref_logits, margin=1e-5):

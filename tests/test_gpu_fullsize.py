@@ -2,27 +2,39 @@
 
 The reference's step is python/orca/nn/model.py:546-552 (zero_grad, forward,
 loss, backward, optimizer step) over Sequential(Linear, ReLU, ..., Linear) +
-CrossEntropyLoss.  These tests hold the tensor-core path to:
+CrossEntropyLoss.
+
+ReLU decisions.  At these sizes some hidden pre-activations lie within
+rounding distance of zero (tens per step among the 33 M of configs[2]).  Any
+correct FP32 summation order -- the reference's matrixmultiply, the oracle's
+k-ascending loop, the tensor cores' -- may give them either sign, and each
+such decision moves a whole gradient column, so comparing gradients against
+the exact (float64) sign pattern would measure those coin flips rather than
+the arithmetic.  These tests therefore read the ReLU pattern the GPU step
+used (orca_mlp_get_activation), require every unit where it differs from the
+exact sign to be a near-tie (|z| <= 1e-5 of the summed magnitudes), and
+compare against float64 computed with that pattern:
 
 * configs[2] at its full 4096-row batch: one step's loss and every gradient
-  within 1e-5 (relative norm) of the exact float64 values, identical argmax
-  (rows without a near-tie), and the SGD-momentum update bit-identical to the
-  oracle's applied to the same gradients;
+  within 1e-5 (relative norm) of float64, identical argmax (rows without a
+  near-tie), and the SGD-momentum update bit-identical to the oracle's applied
+  to the same gradients;
 * 20 teacher-forced steps at the 4096 (configs[1], AdamW) and 8192
-  (configs[2], SGD momentum) widths, 256 rows: at every step the GPU step is
-  evaluated at the oracle's parameters -- loss within 1e-6, every gradient
-  within 1e-5 -- so the K = 4096/8192 chunked accumulation of the products the
-  benchmark times is checked step after step without the chaos of ReLU mask
-  flips (at most one flipped step is allowed);
-* configs[1] at its stated 1024 rows, 20 free-running AdamW steps: loss
-  within 1e-4 every step and parameters within 1e-3, with
-  the number of mask-flip steps counted by a teacher-forced twin and held to
-  at most two;
+  (configs[2], SGD momentum) widths, 256 rows, along the oracle's trajectory:
+  every step's loss within 1e-6 of the oracle's and every gradient within
+  1e-5 of float64 -- the K = 4096/8192 chunked accumulation of the products
+  the benchmark times, step after step;
+* configs[1] at its stated 1024 rows, 20 free-running AdamW steps: the
+  trajectory is chaotic in the reference's own arithmetic (the oracle under
+  its k-ascending GEMM and under matrixmultiply's blocked-FMA order parts by
+  up to ~6e-3 in loss and a few % in parameters), so each step's loss is held
+  to max(1e-4, 2 x that order spread so far) and the final parameters to
+  max(1e-3, 2 x the spread of the same tensor);
 * a configs[4] slice (4096-16384-16384-1000, N(0,1) inputs, 256 rows): loss,
-  logits argmax and every gradient against float64, which covers the
-  16384-wide products and the C = 1000 classifier and softmax-CE.
+  logits argmax and every gradient against float64, covering the 16384-wide
+  products and the C = 1000 classifier and softmax-CE.
 
-The oracle's GEMM runs row-parallel here (bit-identical to its single-thread
+The oracle's GEMM runs multi-threaded here (bit-identical to its single-thread
 order) so these finish in seconds.
 """
 import numpy as np
@@ -30,7 +42,8 @@ import pytest
 
 from oracle import oracle as O
 from orcaml_b200.synthetic import CONFIGS, init_params, make_batch
-from tests.gpu_util import argmax_agrees, f64_forward_backward, rel_err
+from tests.gpu_util import (argmax_agrees, check_mask_flips, f64_forward_backward, gpu_masks,
+                            rel_err)
 
 pytestmark = pytest.mark.gpu
 
@@ -72,12 +85,15 @@ def test_c2_full_batch_step_against_float64(be):
     logits, _ = tr.forward(x, t)
     loss = tr.step(x, t)
     grads = tr.get_grads()
+    masks = gpu_masks(tr)
     stepped = tr.get_parameters()
     tr.close()
-    ref_loss, ref_grads, ref_logits = f64_forward_backward(cfg.dims, params, x, t)
+    ref_loss, ref_grads, ref_logits, pre = f64_forward_backward(cfg.dims, params, x, t, masks)
+    flips = check_mask_flips(masks, pre, x, params)
     assert abs(loss - ref_loss) <= 1e-5 * abs(ref_loss), (loss, ref_loss)
-    for i, (g, r) in enumerate(zip(grads, ref_grads)):
-        assert rel_err(g, r) <= 1e-5, (i, rel_err(g, r))
+    errs = [rel_err(g, r) for g, r in zip(grads, ref_grads)]
+    print(f"c2 4096 rows: gradient errors {[f'{e:.2g}' for e in errs]}, near-tie flips {flips}")
+    assert max(errs) <= 1e-5, errs
     assert argmax_agrees(logits, ref_logits) >= 0.99 * cfg.batch
     # The update: SGD momentum on the GPU's own gradients, first step.
     for i, (p, g) in enumerate(zip(params, grads)):
@@ -93,45 +109,45 @@ def test_teacher_forced_20_steps_at_benchmark_width(be, name):
     x, t, _ = make_batch(dims, B, 0)
     tr = trainer(be, dims, B, "sgd", "tc", lr=0.0)
     ref = O.OracleTrainer(dims, init_params(dims, 1), optimizer=cfg.optimizer, **c_kwargs(cfg))
-    flips, worst = 0, 0.0
+    worst, flips = 0.0, 0
     for step in range(20):
         loss_ref, grads_ref, _ = O.mlp_forward_backward(dims, ref.params, x, t)
         tr.set_parameters(ref.params)
         lg = tr.step(x, t)
         assert abs(lg - loss_ref) <= 1e-6 * abs(loss_ref), (step, lg, loss_ref)
-        errs = [rel_err(g, r) for g, r in zip(tr.get_grads(), grads_ref)]
-        if max(errs) > 1e-5:
-            flips += 1
-        else:
-            worst = max(worst, max(errs))
+        masks = gpu_masks(tr)
+        _, exact, _, pre = f64_forward_backward(dims, ref.params, x, t, masks)
+        flips += check_mask_flips(masks, pre, x, ref.params)
+        errs = [rel_err(g, r) for g, r in zip(tr.get_grads(), exact)]
+        assert max(errs) <= 1e-5, (step, errs)
+        worst = max(worst, max(errs))
         ref.apply(grads_ref)
     tr.close()
-    print(f"{name} width {dims[1]}: worst gradient error {worst:.3g}, mask-flip steps {flips}")
-    assert flips <= 1
+    print(f"{name} width {dims[1]}: worst gradient error {worst:.3g}, near-tie flips {flips}")
 
 
 def test_c1_full_batch_20_free_running_steps(be):
     cfg = CONFIGS["c1"]
     dims, B = cfg.dims, cfg.batch
     x, t, _ = make_batch(dims, B, 0)
+    runs = []
+    for order in (0, 4):                     # two valid FP32 orders of the reference
+        O.set_gemm_order(order)
+        ref = O.OracleTrainer(dims, init_params(dims, 1), optimizer="adamw", **c_kwargs(cfg))
+        runs.append(([ref.step(x, t) for _ in range(20)], ref.params))
+    O.set_gemm_order(0)
+    (l0, p0), (l4, p4) = runs
     free = trainer(be, dims, B, "adamw", **c_kwargs(cfg))
-    forced = trainer(be, dims, B, "sgd", lr=0.0)
-    ref = O.OracleTrainer(dims, init_params(dims, 1), optimizer="adamw", **c_kwargs(cfg))
-    flips = 0
+    spread = 0.0
     for step in range(20):
-        loss_ref, grads_ref, _ = O.mlp_forward_backward(dims, ref.params, x, t)
         lg = free.step(x, t)
-        assert abs(lg - loss_ref) <= 1e-4 * abs(loss_ref), (step, lg, loss_ref)
-        forced.set_parameters(ref.params)
-        forced.step(x, t)
-        if max(rel_err(g, r) for g, r in zip(forced.get_grads(), grads_ref)) > 1e-5:
-            flips += 1
-        ref.apply(grads_ref)
-    errs = [rel_err(p, q) for p, q in zip(free.get_parameters(), ref.params)]
+        spread = max(spread, abs(l4[step] - l0[step]) / abs(l0[step]))
+        bar = max(1e-4, 2.0 * spread)
+        assert abs(lg - l0[step]) <= bar * abs(l0[step]), (step, lg, l0[step], bar)
+    for i, (p, q, r) in enumerate(zip(free.get_parameters(), p0, p4)):
+        bar = max(1e-3, 2.0 * rel_err(r, q))
+        assert rel_err(p, q) <= bar, (i, rel_err(p, q), bar)
     free.close()
-    forced.close()
-    print(f"c1 1024 rows: parameter errors {[f'{e:.2g}' for e in errs]}, mask-flip steps {flips}")
-    assert max(errs) <= 1e-3 and flips <= 2
 
 
 def test_c4_slice_against_float64(be):
@@ -143,8 +159,10 @@ def test_c4_slice_against_float64(be):
     logits, _ = tr.forward(x, t)
     loss = tr.step(x, t)
     grads = tr.get_grads()
+    masks = gpu_masks(tr)
     tr.close()
-    ref_loss, ref_grads, ref_logits = f64_forward_backward(dims, params, x, t)
+    ref_loss, ref_grads, ref_logits, pre = f64_forward_backward(dims, params, x, t, masks)
+    check_mask_flips(masks, pre, x, params)
     assert abs(loss - ref_loss) <= 1e-5 * abs(ref_loss), (loss, ref_loss)
     for i, (g, r) in enumerate(zip(grads, ref_grads)):
         assert rel_err(g, r) <= 1e-5, (i, rel_err(g, r))
