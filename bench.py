@@ -549,6 +549,7 @@ def run_ours(args):
                                    "steps run after the timed ones"},
             "step_tflops": step_flops / (ms_step / 1e3) / 1e12,
             "gpu_launches": int(launches),
+            "exchange": tr.exchange_kind() if comm is not None else None,
             "loss": loss_val,
             "breakdown_ms": breakdown,
             "breakdown_note": f"per launch, from {prof_steps} profiled steps after the timed ones",

@@ -302,8 +302,21 @@ orca_status orca_mlp_set_state(orca_mlp* mlp, int slot, int index, const float* 
  * value (the first momentum step sets v = g, sgd.py:67-71). */
 orca_status orca_mlp_get_step(const orca_mlp* mlp, int64_t* t, int* velocity_started);
 orca_status orca_mlp_set_step(orca_mlp* mlp, int64_t t, int velocity_started);
-/* Attach (or detach with NULL) the communicator used by every later step. */
+/* Attach (or detach with NULL) the communicator used by every later step.
+ * Collective when the peer exchange is chosen (every rank must call it). */
 orca_status orca_mlp_attach_comm(orca_mlp* mlp, orca_comm* comm, size_t bucket_bytes);
+/* How the step averages gradients across ranks (set before attaching; same
+ * on every rank).  NCCL: ncclAllReduce with ncclAvg per bucket.  PEER: the
+ * ranks' gradient arenas are mapped into each other with CUDA IPC and one
+ * kernel per layer sums every element in float64 in rank order and scales
+ * by 1/world -- the reference's average (python/orca/distributed.py:238-256)
+ * bit for bit at every world size -- running on the SMs beside the GEMMs of
+ * the rest of the backward pass.  AUTO: PEER when the mapping can be set up
+ * (world 2..8, CUDA IPC available), else NCCL. */
+typedef enum { ORCA_XCHG_AUTO = 0, ORCA_XCHG_NCCL = 1, ORCA_XCHG_PEER = 2 } orca_exchange;
+orca_status orca_mlp_set_exchange(orca_mlp* mlp, int mode);
+/* The exchange in use: 0 none (no communicator), ORCA_XCHG_NCCL or ORCA_XCHG_PEER. */
+orca_status orca_mlp_exchange_kind(const orca_mlp* mlp, int* kind);
 /* The gradient exchange plan a runner with these dims and bucket size uses
  * (host only; no device needed), replacing the per-parameter loop of
  * DistributedDataParallel.all_reduce_gradients (python/orca/distributed.py:

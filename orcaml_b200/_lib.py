@@ -135,6 +135,8 @@ _SIGS = {
     "orca_mlp_get_grad": ([c_void_p, c_int, c_void_p, c_int64], c_int),
     "orca_mlp_get_activation": ([c_void_p, c_int, c_void_p, c_int64], c_int),
     "orca_mlp_attach_comm": ([c_void_p, c_void_p, c_size_t], c_int),
+    "orca_mlp_set_exchange": ([c_void_p, c_int], c_int),
+    "orca_mlp_exchange_kind": ([c_void_p, ctypes.POINTER(c_int)], c_int),
     "orca_mlp_bucket_plan": ([c_int, P_int64, c_size_t, c_int, P_int64, P_int64,
                               ctypes.POINTER(c_int), ctypes.POINTER(c_int)], c_int),
     "orca_mlp_step": ([c_void_p, c_void_p, c_void_p, c_void_p], c_int),

@@ -18,6 +18,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <thread>
+#include <vector>
 
 #include "common.cuh"
 
@@ -115,6 +116,288 @@ orca_status comm_allreduce_avg_stream(orca_comm* c, float* ptr, size_t n, cudaSt
   ncclResult_t r = a.AllReduce(ptr, ptr, n, ncclFloat32, ncclAvg, c->comm, stream);
   if (r == ncclInProgress) return wait_ready(c, "ncclAllReduce");
   if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce");
+  return ORCA_OK;
+}
+
+// =============================================================== peer exchange
+// The gradient all-reduce of the step runner as a kernel of its own over the
+// ranks' gradient arenas, mapped into every process with CUDA IPC (plain
+// peer loads and stores over NVLink; no multicast).  Why not NCCL: NCCL's
+// kernels need more shared memory than the persistent GEMMs leave on an SM,
+// so the layer-1 all-reduce could start only once the dX GEMM had finished.
+// This kernel uses four warps per block, at most 85 registers per thread and
+// no dynamic shared memory, so its blocks fit on the SMs next to the GEMM's
+// CTAs and the exchange runs while the GEMM computes.
+//
+// It also restates the reference's average exactly
+// (python/orca/distributed.py:238-256): each element is summed in float64 in
+// rank order, multiplied by 1/world in float64 and rounded once to float32 --
+// bit for bit the reference's result at every world size (NCCL's ncclAvg
+// differs from it in the last bits at world > 2).
+//
+// Protocol for one range [offset, offset + n) of the arena (one layer), on
+// the comm stream after the range's gradients are complete:
+//   1. peer_signal_kernel: ready[slot][rank] = seq on every rank;
+//   2. peer_reduce_kernel: every block waits until ready[slot][r] >= seq for
+//      all r (bounded), then reduces its part of this rank's chunk
+//      (n / world floats): loads the chunk from every rank's arena, sums in
+//      rank order and stores the average into every rank's arena; the last
+//      block to finish sets done[slot][rank] = seq on every rank and waits
+//      until done[slot][r] >= seq for all r -- when the kernel completes,
+//      every rank's averaged chunk has landed in this rank's arena.
+// seq grows by one per step on every rank.  All waits are bounded
+// (limit_ns); a wait that runs out sets the device error word, skips the
+// rest and signals nothing, so the peers' waits run out too and every rank's
+// step reports ORCA_TIMEOUT.
+constexpr int kMaxPeers = 8;
+constexpr int kPeerThreads = 128;
+
+struct PeerArgs {
+  float* base[kMaxPeers];       // arena base on every rank (own pointer at [rank])
+  uint32_t* flags[kMaxPeers];   // flag array on every rank: [slot][ready, done][src]
+  int world = 1, rank = 0, slot = 0;
+  uint32_t seq = 0;
+  int64_t offset = 0, n = 0;    // the range, in floats from the arena base
+  unsigned* counter = nullptr;  // this rank's finished-block counter of the slot
+  int* dev_err = nullptr;
+  uint64_t limit_ns = 0;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t* peer_flag(uint32_t* base, int slot, int phase, int src) {
+  return base + ((size_t)slot * 2 + phase) * kMaxPeers + src;
+}
+
+// Waits until every rank's flag (slot, phase) in this rank's array reaches
+// seq (wrap-safe); false after limit_ns, with the device error word set.
+__device__ bool peer_wait_all(const PeerArgs& a, int phase) {
+  const uint64_t t0 = global_ns();
+  for (int r = 0; r < a.world; ++r) {
+    const uint32_t* f = peer_flag(a.flags[a.rank], a.slot, phase, r);
+    unsigned polls = 0;
+    while ((int32_t)(ld_acquire_sys(f) - a.seq) < 0) {
+      if ((++polls & 63u) == 0 && global_ns() - t0 > a.limit_ns) {
+        atomicExch(a.dev_err, DEV_WAIT_TIMEOUT);
+        return false;
+      }
+      __nanosleep(200);
+    }
+  }
+  return true;
+}
+
+__global__ void peer_signal_kernel(PeerArgs a, int phase) {
+  __threadfence_system();
+  const int r = threadIdx.x;
+  if (r < a.world) st_release_sys(peer_flag(a.flags[r], a.slot, phase, a.rank), a.seq);
+}
+
+// out = float32(((double)x[0] + x[1] + ... + x[world-1]) * inv_w)
+__device__ __forceinline__ float peer_avg(const float (&x)[kMaxPeers], int world, double inv_w) {
+  double s = (double)x[0];
+#pragma unroll
+  for (int r = 1; r < kMaxPeers; ++r)
+    if (r < world) s = __dadd_rn(s, (double)x[r]);
+  return __double2float_rn(__dmul_rn(s, inv_w));
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(kPeerThreads, 6) peer_reduce_kernel(PeerArgs a, double inv_w) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = peer_wait_all(a, 0) ? 1 : 0;
+  __syncthreads();
+  if (ok) {
+    const int64_t per = (cdiv(a.n, (int64_t)a.world) + 3) & ~int64_t(3);
+    const int64_t c0 = std::min<int64_t>(a.n, (int64_t)a.rank * per);
+    const int64_t c1 = std::min<int64_t>(a.n, c0 + per);
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    int64_t tail = c0;
+    if (kVec) {
+      const int64_t nv = (c1 - c0) / 4;
+      for (int64_t v = tid; v < nv; v += nthreads) {
+        const int64_t i = a.offset + c0 + 4 * v;
+        float4 x[kMaxPeers];
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r)
+          if (r < a.world) x[r] = __ldcg(reinterpret_cast<const float4*>(a.base[r] + i));
+        float e[kMaxPeers];
+        float4 o;
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? x[r].x : 0.0f;
+        o.x = peer_avg(e, a.world, inv_w);
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? x[r].y : 0.0f;
+        o.y = peer_avg(e, a.world, inv_w);
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? x[r].z : 0.0f;
+        o.z = peer_avg(e, a.world, inv_w);
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? x[r].w : 0.0f;
+        o.w = peer_avg(e, a.world, inv_w);
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r)
+          if (r < a.world) __stcg(reinterpret_cast<float4*>(a.base[r] + i), o);
+      }
+      tail = c0 + 4 * nv;
+    }
+    for (int64_t j = tail + tid; j < c1; j += nthreads) {
+      const int64_t i = a.offset + j;
+      float e[kMaxPeers];
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? __ldcg(a.base[r] + i) : 0.0f;
+      const float o = peer_avg(e, a.world, inv_w);
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        if (r < a.world) __stcg(a.base[r] + i, o);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(a.counter, 1u);
+    if (prev == gridDim.x - 1) {
+      *a.counter = 0;   // every block has counted: ready for the slot's next use
+      if (atomicAdd(a.dev_err, 0) == DEV_OK) {
+        __threadfence_system();
+        for (int r = 0; r < a.world; ++r)
+          st_release_sys(peer_flag(a.flags[r], a.slot, 1, a.rank), a.seq);
+        peer_wait_all(a, 1);
+      }
+    }
+  }
+}
+
+struct PeerArena {
+  orca_comm* comm = nullptr;
+  PeerArgs args;                 // base, flags, world, rank, dev_err, limit_ns
+  int n_slots = 0;
+  uint32_t* flags = nullptr;     // this rank's flag array (exported)
+  unsigned* counters = nullptr;  // [n_slots], local
+  std::vector<void*> opened;     // peers' mappings
+};
+
+void peer_arena_close(PeerArena* pa) {
+  if (!pa) return;
+  for (void* p : pa->opened) cudaIpcCloseMemHandle(p);
+  if (pa->flags) cudaFree(pa->flags);
+  if (pa->counters) cudaFree(pa->counters);
+  delete pa;
+}
+
+orca_status peer_arena_open(orca_comm* c, float* base, int n_slots, PeerArena** out) {
+  *out = nullptr;
+  if (!c || c->aborted) return fail(ORCA_COMM_ERROR, "communicator unavailable");
+  if (c->world < 2 || c->world > kMaxPeers)
+    return fail(ORCA_INVALID_ARGUMENT, "peer exchange: world %d not in [2, %d]", c->world,
+                kMaxPeers);
+  if (n_slots < 1) return fail(ORCA_INVALID_ARGUMENT, "peer exchange: no slots");
+  orca_ctx* ctx = c->ctx;
+  NcclApi& nc = api();
+  PeerArena* pa = new PeerArena();
+  pa->comm = c;
+  pa->n_slots = n_slots;
+  struct Guard {
+    PeerArena*& pa;
+    ~Guard() { if (pa) peer_arena_close(pa); }
+  } guard{pa};
+  const size_t flag_bytes = (size_t)n_slots * 2 * kMaxPeers * sizeof(uint32_t);
+  ORCA_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&pa->flags), flag_bytes));
+  ORCA_CUDA_TRY(cudaMemset(pa->flags, 0, flag_bytes));
+  ORCA_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&pa->counters), (size_t)n_slots * 4));
+  ORCA_CUDA_TRY(cudaMemset(pa->counters, 0, (size_t)n_slots * 4));
+  // Exchange the two IPC handles and the device UUID of every rank through
+  // the communicator: a byte-wise sum over a buffer in which each rank fills
+  // only its own slot.
+  struct Entry {
+    cudaIpcMemHandle_t h[2];
+    cudaUUID_t uuid;
+  } mine;
+  ORCA_CUDA_TRY(cudaIpcGetMemHandle(&mine.h[0], base));
+  ORCA_CUDA_TRY(cudaIpcGetMemHandle(&mine.h[1], pa->flags));
+  cudaDeviceProp prop;
+  ORCA_CUDA_TRY(cudaGetDeviceProperties(&prop, ctx->device));
+  mine.uuid = prop.uuid;
+  const size_t hb = sizeof(mine);
+  std::vector<uint8_t> handles((size_t)c->world * hb, 0);
+  memcpy(handles.data() + (size_t)c->rank * hb, &mine, hb);
+  uint8_t* dbuf = nullptr;
+  ORCA_CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&dbuf), handles.size()));
+  struct FreeBuf {
+    uint8_t* p;
+    ~FreeBuf() { cudaFree(p); }
+  } free_buf{dbuf};
+  ORCA_CUDA_TRY(cudaMemcpy(dbuf, handles.data(), handles.size(), cudaMemcpyHostToDevice));
+  ncclResult_t r = nc.AllReduce(dbuf, dbuf, handles.size(), ncclUint8, ncclSum, c->comm,
+                                ctx->comm_stream);
+  if (r == ncclInProgress) ORCA_TRY(wait_ready(c, "ncclAllReduce (IPC handles)"));
+  else if (r != ncclSuccess) return nccl_fail(r, "ncclAllReduce (IPC handles)");
+  ORCA_TRY(sync_stream_for(ctx, ctx->comm_stream, c->timeout_s));
+  ORCA_CUDA_TRY(cudaMemcpy(handles.data(), dbuf, handles.size(), cudaMemcpyDeviceToHost));
+  // Every rank must own its GPU: the exchange kernels of different ranks
+  // wait on one another, which only works when they run on different devices.
+  for (int q = 0; q < c->world; ++q) {
+    Entry e;
+    memcpy(&e, handles.data() + (size_t)q * hb, hb);
+    if (q != c->rank && memcmp(&e.uuid, &mine.uuid, sizeof(cudaUUID_t)) == 0)
+      return fail(ORCA_INVALID_ARGUMENT, "peer exchange: ranks %d and %d share a GPU", c->rank, q);
+  }
+  for (int q = 0; q < c->world; ++q) {
+    if (q == c->rank) {
+      pa->args.base[q] = base;
+      pa->args.flags[q] = pa->flags;
+      continue;
+    }
+    Entry e;
+    memcpy(&e, handles.data() + (size_t)q * hb, hb);
+    void* pb = nullptr;
+    void* pf = nullptr;
+    ORCA_CUDA_TRY(cudaIpcOpenMemHandle(&pb, e.h[0], cudaIpcMemLazyEnablePeerAccess));
+    pa->opened.push_back(pb);
+    ORCA_CUDA_TRY(cudaIpcOpenMemHandle(&pf, e.h[1], cudaIpcMemLazyEnablePeerAccess));
+    pa->opened.push_back(pf);
+    pa->args.base[q] = static_cast<float*>(pb);
+    pa->args.flags[q] = static_cast<uint32_t*>(pf);
+  }
+  pa->args.world = c->world;
+  pa->args.rank = c->rank;
+  pa->args.dev_err = ctx->dev_err;
+  pa->args.limit_ns = (uint64_t)(std::min(c->timeout_s, 60.0) * 1e9);
+  *out = pa;
+  pa = nullptr;   // keep it
+  return ORCA_OK;
+}
+
+orca_status peer_arena_allreduce_avg(PeerArena* pa, int slot, int64_t offset, int64_t n,
+                                     uint32_t seq, cudaStream_t stream) {
+  if (!pa || slot < 0 || slot >= pa->n_slots || n < 0 || offset < 0)
+    return fail(ORCA_INVALID_ARGUMENT, "peer exchange: bad range");
+  if (n == 0) return ORCA_OK;
+  PeerArgs a = pa->args;
+  a.slot = slot;
+  a.seq = seq;
+  a.offset = offset;
+  a.n = n;
+  a.counter = pa->counters + slot;
+  orca_ctx* ctx = pa->comm->ctx;
+  peer_signal_kernel<<<1, 32, 0, stream>>>(a, 0);
+  const int64_t per = (cdiv(n, (int64_t)a.world) + 3) & ~int64_t(3);
+  const int grid =
+      (int)std::max<int64_t>(1, std::min<int64_t>(ctx->sm_count, cdiv(per, 4 * kPeerThreads)));
+  const double inv_w = 1.0 / (double)a.world;
+  if ((offset & 3) == 0)
+    peer_reduce_kernel<true><<<grid, kPeerThreads, 0, stream>>>(a, inv_w);
+  else
+    peer_reduce_kernel<false><<<grid, kPeerThreads, 0, stream>>>(a, inv_w);
+  count_launch(ctx, 2);
+  ORCA_CUDA_TRY(cudaGetLastError());
   return ORCA_OK;
 }
 

@@ -23,6 +23,15 @@ namespace orca {
 // ---------------------------------------------------------------- host status
 void set_error(const char* fmt, ...);
 orca_status fail(orca_status s, const char* fmt, ...);
+// Gradient exchange over peer memory (comm.cu): the arena `base` (a cudaMalloc
+// allocation of every rank, same layout) is mapped into every rank's process;
+// peer_arena_allreduce_avg averages [offset, offset + n) of it across ranks,
+// enqueued on `stream`; seq must grow by one per use of a slot on every rank.
+struct PeerArena;
+orca_status peer_arena_open(orca_comm* c, float* base, int n_slots, PeerArena** out);
+orca_status peer_arena_allreduce_avg(PeerArena* pa, int slot, int64_t offset, int64_t n,
+                                     uint32_t seq, cudaStream_t stream);
+void peer_arena_close(PeerArena* pa);
 // Looks up, once per device, the device address of the fixed scratch array of
 // orca_softmax_ce_fwd_bwd_noalloc (mlp.cu); the device must be current.
 orca_status ce_scratch_setup(int device);

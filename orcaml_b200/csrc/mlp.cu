@@ -574,6 +574,9 @@ struct orca_mlp {
   // data parallel
   orca_comm* comm = nullptr;
   size_t bucket_bytes = 0;
+  int xchg_mode = ORCA_XCHG_AUTO;   // requested exchange (orca_mlp_set_exchange)
+  PeerArena* pex = nullptr;         // peer exchange of the gradient arena, when in use
+  uint32_t pex_seq = 0;             // steps exchanged through pex (same on every rank)
   cudaEvent_t ev_layer[64];         // layer's gradients ready (compute stream)
   cudaEvent_t ev_reduced[64];       // layer's gradients averaged (comm stream)
   int last_launches = 0;
@@ -833,6 +836,7 @@ orca_status orca_mlp_destroy(orca_mlp* m) {
     if (m->ev_consumed[i]) cudaEventDestroy(m->ev_consumed[i]);
   }
   if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
+  if (m->pex) peer_arena_close(m->pex);   // before the arena it maps is freed
   for (void* p : m->allocs) cudaFree(p);
   if (m->host_stage) cudaFreeHost(m->host_stage);
   for (int l = 0; l < 64; ++l)
@@ -1011,11 +1015,61 @@ orca_status orca_mlp_bucket_plan(int n_layers, const int64_t* dims, size_t bucke
   return ORCA_OK;
 }
 
+// Whether AUTO takes the peer exchange when it can be set up.
+constexpr bool kAutoPeer = false;
+// ORCA_XCHG=nccl|peer overrides the automatic choice (for measurements).
+static int xchg_env() {
+  static const int v = [] {
+    const char* e = getenv("ORCA_XCHG");
+    if (e && strcmp(e, "nccl") == 0) return (int)ORCA_XCHG_NCCL;
+    if (e && strcmp(e, "peer") == 0) return (int)ORCA_XCHG_PEER;
+    return (int)ORCA_XCHG_AUTO;
+  }();
+  return v;
+}
+
+orca_status orca_mlp_set_exchange(orca_mlp* m, int mode) {
+  if (!m) return fail(ORCA_INVALID_ARGUMENT, "null mlp");
+  if (mode < ORCA_XCHG_AUTO || mode > ORCA_XCHG_PEER)
+    return fail(ORCA_INVALID_ARGUMENT, "exchange mode %d", mode);
+  if (m->comm) return fail(ORCA_INVALID_ARGUMENT, "set the exchange before attaching a communicator");
+  m->xchg_mode = mode;
+  return ORCA_OK;
+}
+
+orca_status orca_mlp_exchange_kind(const orca_mlp* m, int* kind) {
+  if (!m || !kind) return fail(ORCA_INVALID_ARGUMENT, "null argument");
+  *kind = !m->comm ? 0 : (m->pex ? (int)ORCA_XCHG_PEER : (int)ORCA_XCHG_NCCL);
+  return ORCA_OK;
+}
+
 orca_status orca_mlp_attach_comm(orca_mlp* m, orca_comm* comm, size_t bucket_bytes) {
   if (!m) return fail(ORCA_INVALID_ARGUMENT, "null mlp");
+  if (m->pex) {
+    // No exchange of the old communicator may still be running.
+    ORCA_TRY(sync_stream_for(m->ctx, m->ctx->comm_stream, m->ctx->sync_timeout_s));
+    ORCA_TRY(sync_stream_for(m->ctx, m->ctx->stream, m->ctx->sync_timeout_s));
+    peer_arena_close(m->pex);
+    m->pex = nullptr;
+  }
   m->comm = comm;
   m->bucket_bytes = bucket_bytes;
-  return ORCA_OK;
+  m->pex_seq = 0;
+  if (!comm) return ORCA_OK;
+  const int env = xchg_env();
+  const int mode = env != ORCA_XCHG_AUTO ? env : m->xchg_mode;
+  if (mode == ORCA_XCHG_NCCL || (mode == ORCA_XCHG_AUTO && !kAutoPeer)) return ORCA_OK;
+  ORCA_TRY(check_ctx(m->ctx));
+  std::lock_guard<std::mutex> lk(m->ctx->mu);
+  ORCA_TRY(sync_stream_for(m->ctx, m->ctx->stream, m->ctx->sync_timeout_s));
+  // Every rank opens (collective: the IPC handles travel through the
+  // communicator), so every rank must request the same mode.
+  const orca_status s = peer_arena_open(comm, m->grads, m->L, &m->pex);
+  if (s != ORCA_OK && mode == ORCA_XCHG_PEER) {
+    m->comm = nullptr;
+    return s;
+  }
+  return ORCA_OK;   // AUTO: NCCL when the peer mapping is unavailable
 }
 
 // One step on device inputs.  inputs_read (nullable) is recorded on the
@@ -1400,6 +1454,17 @@ static orca_status launch_layer_allreduce(orca_mlp* m, int l) {
   orca_ctx* ctx = m->ctx;
   ORCA_CUDA_TRY(cudaEventRecord(m->ev_layer[l], ctx->stream));
   ORCA_CUDA_TRY(cudaStreamWaitEvent(ctx->comm_stream, m->ev_layer[l], 0));
+  if (m->pex) {
+    // The whole layer in one exchange (its kernel runs beside the GEMMs).
+    const int64_t n = m->dims[l] * m->dims[l + 1] + m->dims[l + 1];
+    const int pr = prof_open(m, "allreduce_l" + std::to_string(l), 0.0, 4.0 * (double)n, -1,
+                             ctx->comm_stream);
+    ORCA_TRY(peer_arena_allreduce_avg(m->pex, l, m->p_off[2 * l], n, m->pex_seq,
+                                      ctx->comm_stream));
+    prof_close(m, pr);
+    ORCA_CUDA_TRY(cudaEventRecord(m->ev_reduced[l], ctx->comm_stream));
+    return ORCA_OK;
+  }
   std::vector<Bucket> plan;
   bucket_plan(m->L, m->dims.data(), m->bucket_bytes, plan);
   // Timed on the comm stream: from the layer's gradients being ready to
@@ -1421,6 +1486,7 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
   orca_ctx* ctx = m->ctx;
   const int L = m->L;
   const int64_t B = m->B;
+  if (m->pex) ++m->pex_seq;
   // g: gradient w.r.t. the current layer's pre-activation output.
   const float* g_hi = m->dlogits;
   const float* g_lo = nullptr;

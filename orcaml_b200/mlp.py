@@ -328,6 +328,22 @@ class MlpTrainer:
                         "flops": fl.value, "bytes": by.value, "gemm_path": path.value})
         return out
 
+    EXCHANGE = {"auto": 0, "nccl": 1, "peer": 2}
+
+    def set_exchange(self, mode: str):
+        """How gradients are averaged across ranks once a communicator is
+        attached: "nccl" (ncclAllReduce, ncclAvg), "peer" (one kernel per
+        layer over the ranks' IPC-mapped gradient arenas, float64 rank-order
+        sum: the reference's average bit for bit) or "auto"."""
+        if mode not in self.EXCHANGE:
+            raise ValueError(f"exchange must be one of {sorted(self.EXCHANGE)}")
+        L.check(L.load().orca_mlp_set_exchange(self._h, self.EXCHANGE[mode]))
+
+    def exchange_kind(self) -> str:
+        k = ctypes.c_int()
+        L.check(L.load().orca_mlp_exchange_kind(self._h, ctypes.byref(k)))
+        return {0: "none", 1: "nccl", 2: "peer"}[k.value]
+
     def attach_comm(self, comm, bucket_bytes: int = 0):
         self._comm = comm
         L.check(L.load().orca_mlp_attach_comm(self._h, comm.handle if comm is not None else None,

@@ -54,17 +54,19 @@ def _gpus():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("xchg", ["nccl", "peer"])
 @pytest.mark.parametrize("opt,dims,batch,path", [("adamw", [784, 256, 256, 10], 64, "auto"),
                                                  ("sgd", [784, 1024, 1024, 10], 512, "tc")])
-def test_ddp_two_gpus_matches_oracle(tmp_path, opt, dims, batch, path):
-    """The "tc" case runs the hidden layers on the tensor cores, so the dX GEMM
+def test_ddp_two_gpus_matches_oracle(tmp_path, opt, dims, batch, path, xchg):
+    """Both exchanges (NCCL all-reduce; the peer-memory kernel).  The "tc"
+    case runs the hidden layers on the tensor cores, so with NCCL the dX GEMM
     after each gradient all-reduce is split into two launches (the first on
     fewer CTAs, leaving SMs to the collective)."""
     from oracle import oracle as O
     from orcaml_b200.synthetic import init_params, make_batch
-    steps, world, port = 10, 2, 29411 + batch
+    steps, world, port = 10, 2, 29411 + batch + (0 if xchg == "nccl" else 3)
     code = f"REPO = {REPO!r}\nOUT = {str(tmp_path)!r}\n" + WORKER
-    env = dict(os.environ, ORCA_COMM_SMS="16")   # exercise the split dX GEMM
+    env = dict(os.environ, ORCA_COMM_SMS="16", ORCA_XCHG=xchg)   # exercise the split dX GEMM
     procs = [subprocess.Popen([sys.executable, "-c", code, str(r), str(world), str(port),
                                json.dumps(dims), str(batch), str(steps), opt, path], env=env)
              for r in range(world)]
@@ -141,17 +143,19 @@ be.close()
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("xchg", ["nccl", "peer"])
 @pytest.mark.parametrize("mode", ["exit", "stall"])
-def test_ddp_peer_loss_raises_instead_of_hanging(tmp_path, mode):
+def test_ddp_peer_loss_raises_instead_of_hanging(tmp_path, mode, xchg):
     """A peer that exits between steps is seen on the rendezvous sockets before
     the next step launches anything ("exit"); a peer that stays but never joins
     the next step makes the all-reduce miss the 10 s deadline, the
-    communicator is aborted ("stall").  Either way the surviving rank gets
+    communicator is aborted ("stall"); with the peer exchange the survivor's
+    kernel gives up its bounded wait for the peer's ready flag.  Either way the surviving rank gets
     RuntimeError, well before any outer bound, and exits cleanly.  NVLS is off
     (NCCL_NVLS_ENABLE=0) so no rank's memory is bound to a multicast object."""
-    port = 29611 + (0 if mode == "exit" else 7)
+    port = 29611 + (0 if mode == "exit" else 7) + (0 if xchg == "nccl" else 20)
     code = f"REPO = {REPO!r}\nOUT = {str(tmp_path)!r}\nTIMEOUT = 10.0\n" + LEAVER
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", ORCA_XCHG=xchg)
     procs = [subprocess.Popen([sys.executable, "-c", code, str(r), str(port), mode], env=env)
              for r in range(2)]
     try:
@@ -171,3 +175,67 @@ def test_ddp_peer_loss_raises_instead_of_hanging(tmp_path, mode):
         assert "closed its connection" in res["raised"] and res["elapsed"] < 5.0
     else:
         assert "stopped responding" in res["raised"] and 9.0 <= res["elapsed"] < 60.0
+
+
+EXACT = r"""
+import json, sys
+import numpy as np
+sys.path.insert(0, REPO)
+from orcaml_b200.backend import CudaBackend
+from orcaml_b200.mlp import MlpTrainer
+from orcaml_b200.distributed import DistributedDataParallel
+from orcaml_b200.synthetic import init_params, make_batch
+rank, world, port, xchg = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]), sys.argv[4]
+dims, B = [784, 1024, 1024, 10], 512
+be = CudaBackend(rank)
+x, t, _ = make_batch(dims, B, rank)
+solo = MlpTrainer(be, dims, B, optimizer="sgd", lr=0.0, gemm_path="tc")
+solo.set_parameters(init_params(dims, 1))
+solo.step(x, t)
+np.savez(OUT + f"/local{rank}.npz", *solo.get_grads())
+solo.close()
+tr = MlpTrainer(be, dims, B, optimizer="sgd", lr=0.0, gemm_path="tc")
+tr.set_exchange(xchg)
+tr.set_parameters(init_params(dims, 1))
+ddp = DistributedDataParallel(tr, rank=rank, world_size=world, master_addr=f"127.0.0.1:{port}",
+                              timeout=60.0)
+for _ in range(3):                    # lr 0: the same gradients every step
+    ddp.step(x, t)
+kind = tr.exchange_kind()
+np.savez(OUT + f"/avg{rank}.npz", *tr.get_grads())
+json.dump(kind, open(OUT + f"/kind{rank}.json", "w"))
+ddp.close()
+"""
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("xchg", ["nccl", "peer"])
+def test_exchange_is_the_reference_average_bit_for_bit(tmp_path, xchg):
+    """Each rank's averaged gradients equal, bit for bit, the reference's
+    average (python/orca/distributed.py:238-256: float64 sum in rank order,
+    x 1/world, rounded to float32; oracle.ddp_average) of the ranks' own local
+    gradients (computed by a trainer without a communicator: the kernels are
+    deterministic, so they are the gradients the exchange received), on three
+    consecutive steps (the peer exchange's sequence numbers advance)."""
+    from oracle import oracle as O
+    world, port = 2, 29711 + (0 if xchg == "nccl" else 5)
+    code = f"REPO = {REPO!r}\nOUT = {str(tmp_path)!r}\n" + EXACT
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, "-c", code, str(r), str(world), str(port), xchg],
+                              env=env) for r in range(world)]
+    try:
+        for p in procs:
+            assert p.wait(timeout=600) == 0
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+                p.wait(timeout=60)
+    local = [np.load(tmp_path / f"local{r}.npz") for r in range(world)]
+    avg = [np.load(tmp_path / f"avg{r}.npz") for r in range(world)]
+    for r in range(world):
+        assert json.load(open(tmp_path / f"kind{r}.json")) == xchg
+    for i in range(len(local[0].files)):
+        ref = O.ddp_average([local[r][f"arr_{i}"] for r in range(world)])
+        for r in range(world):
+            assert np.array_equal(avg[r][f"arr_{i}"], ref), (i, r)
