@@ -327,6 +327,7 @@ struct Params {
   int a_load, b_load;      // LOAD_* mode of each operand's tensor map
   int64_t tile_begin, tile_end;   // tiles [tile_begin, tile_end) of the raster order
   int group_m;             // tile rows per raster group (consecutive tiles share B columns)
+  int load_evict_last;     // operand loads carry an L2 evict-last policy
 };
 
 // Dynamic tile scheduling of tc_gemm_kernel: the producer takes the next tile
@@ -386,7 +387,19 @@ __device__ __forceinline__ void tile_coords(int64_t tile, int64_t num_m, int64_t
 constexpr int LOAD_K = 0, LOAD_MN_CHUNKS = 1, LOAD_MN_4D = 2;
 
 __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* map, uint64_t* bar,
-                                             int mode, int rows, int64_t mn0, int64_t k0) {
+                                             int mode, int rows, int64_t mn0, int64_t k0,
+                                             uint64_t policy = 0) {
+  if (policy) {
+    if (mode == LOAD_MN_4D) {
+      tma_load_4d_hint(dst, map, bar, 0, (int)k0, 0, (int)(mn0 / 32), policy);
+    } else if (mode == LOAD_MN_CHUNKS) {
+      for (int c = 0; c < rows / 32; ++c)
+        tma_load_3d_hint(dst + c * 4096, map, bar, (int)(mn0 + 32 * c), (int)k0, 0, policy);
+    } else {
+      tma_load_3d_hint(dst, map, bar, (int)k0, (int)mn0, 0, policy);
+    }
+    return;
+  }
   if (mode == LOAD_MN_4D) {
     tma_load_4d(dst, map, bar, 0, (int)k0, 0, (int)(mn0 / 32));
   } else if (mode == LOAD_MN_CHUNKS) {
@@ -476,6 +489,7 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
     return;
   }
   const int64_t base = m * ep.ldc + n0;
+  const uint64_t spol = ep.store_evict_first ? l2_policy_evict_first() : 0;
   if (ep.mode == EPI_STORE || ep.mode == EPI_BIAS) {
     float4* o = reinterpret_cast<float4*>(ep.out + base);
 #pragma unroll
@@ -488,7 +502,8 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
         r.z = __fadd_rn(r.z, ep.bias[n0 + 4 * q + 2]);
         r.w = __fadd_rn(r.w, ep.bias[n0 + 4 * q + 3]);
       }
-      o[q] = r;
+      if (spol) st_global_v4_hint(o + q, r, spol);
+      else o[q] = r;
     }
     return;
   }
@@ -518,8 +533,13 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
     split_tf32(x[1], h.y, l.y);
     split_tf32(x[2], h.z, l.z);
     split_tf32(x[3], h.w, l.w);
-    oh[q] = h;
-    ol[q] = l;
+    if (spol) {
+      st_global_v4_hint(oh + q, h, spol);
+      st_global_v4_hint(ol + q, l, spol);
+    } else {
+      oh[q] = h;
+      ol[q] = l;
+    }
   }
 }
 #undef v
@@ -582,6 +602,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      const uint64_t policy = p.load_evict_last ? l2_policy_evict_last() : 0;
       int stage = 0;
       uint32_t phase = 0;
       int issued[STAGES];
@@ -603,9 +624,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.dev_err, 20)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[stage], A_STAGE + B_STAGE);
           load_operand(a_tiles + stage * A_STAGE, &map_a, &full_bar[stage], p.a_load, BM, tm * BM,
-                       kb * BK);
+                       kb * BK, policy);
           load_operand(b_tiles + stage * B_STAGE, &map_b, &full_bar[stage], p.b_load, BN, tn * BN,
-                       kb * BK);
+                       kb * BK, policy);
           issued[stage] = (int)phase;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -1251,6 +1272,18 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
     return (int)(v > 0 ? v : GROUP_M);
   }();
   p.group_m = group_m;
+  // L2 policies (ORCA_GEMM_L2HINT, a bit mask): 1 = operand loads
+  // evict-last when both operands fit in three quarters of the L2 (the output
+  // then streams past them), 2 = output stores evict-first.
+  static const int l2hint = [] {
+    const char* e = getenv("ORCA_GEMM_L2HINT");
+    return e ? (int)strtol(e, nullptr, 10) : 0;
+  }();
+  {
+    const double opnd = 8.0 * ((double)M * K + (double)K * N);   // both planes of both
+    p.load_evict_last = ((l2hint & 1) && opnd < 96e6) ? 1 : 0;
+    p.ep.store_evict_first = (l2hint & 2) ? 1 : 0;
+  }
   // Measured on B200 (mean |error| / sum|a*b|, relu-activation x weight data):
   // 8 k-blocks per chunk gives 1.6e-8 at K = 8192 and 5e-8 at K = 784, 4 gives
   // 2.6e-8 at K = 784; a single chain gives 1.0e-6 at K = 8192.  Serial FP32

@@ -45,6 +45,9 @@ struct Epilogue {
   int dot_n = 0;
   float* dot_out = nullptr;
   int64_t dot_ldp = 0;
+  // Tensor-core path: full 128-bit output stores carry an L2 evict-first
+  // policy (the output streams past the operands instead of evicting them).
+  int store_evict_first = 0;
 };
 
 // Columns of the activation covered by one dot_out slice.
