@@ -208,7 +208,10 @@ __device__ __forceinline__ float peer_avg(const float (&x)[kMaxPeers], int world
   return __double2float_rn(__dmul_rn(s, inv_w));
 }
 
-template <bool kVec>
+// kU float4 vectors per thread and iteration: the loads of all kU x world
+// vectors are issued before any is summed, so a thread keeps kU x world x 16
+// bytes in flight (128 bytes at every world size: kU = 8 / world).
+template <bool kVec, int kU>
 __global__ void __launch_bounds__(kPeerThreads, 6) peer_reduce_kernel(PeerArgs a, double inv_w) {
   __shared__ int ok;
   if (threadIdx.x == 0) ok = peer_wait_all(a, 0) ? 1 : 0;
@@ -221,30 +224,41 @@ __global__ void __launch_bounds__(kPeerThreads, 6) peer_reduce_kernel(PeerArgs a
     const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
     int64_t tail = c0;
     if (kVec) {
+      constexpr int R = kMaxPeers / kU;   // ranks this instance can hold (world <= R)
       const int64_t nv = (c1 - c0) / 4;
-      for (int64_t v = tid; v < nv; v += nthreads) {
-        const int64_t i = a.offset + c0 + 4 * v;
-        float4 x[kMaxPeers];
+      for (int64_t v0 = tid; v0 < nv; v0 += nthreads * kU) {
+        float4 x[kU][R];
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r)
-          if (r < a.world) x[r] = __ldcg(reinterpret_cast<const float4*>(a.base[r] + i));
-        float e[kMaxPeers];
-        float4 o;
+        for (int u = 0; u < kU; ++u) {
+          const int64_t v = v0 + (int64_t)u * nthreads;
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? x[r].x : 0.0f;
-        o.x = peer_avg(e, a.world, inv_w);
+          for (int r = 0; r < R; ++r)
+            if (r < a.world && v < nv)
+              x[u][r] = __ldcg(reinterpret_cast<const float4*>(a.base[r] + a.offset + c0 + 4 * v));
+        }
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? x[r].y : 0.0f;
-        o.y = peer_avg(e, a.world, inv_w);
+        for (int u = 0; u < kU; ++u) {
+          const int64_t v = v0 + (int64_t)u * nthreads;
+          if (v >= nv) break;
+          float e[kMaxPeers];
+          float4 o;
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? x[r].z : 0.0f;
-        o.z = peer_avg(e, a.world, inv_w);
+          for (int r = 0; r < kMaxPeers; ++r) e[r] = (r < R && r < a.world) ? x[u][r < R ? r : 0].x : 0.0f;
+          o.x = peer_avg(e, a.world, inv_w);
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r) e[r] = r < a.world ? x[r].w : 0.0f;
-        o.w = peer_avg(e, a.world, inv_w);
+          for (int r = 0; r < kMaxPeers; ++r) e[r] = (r < R && r < a.world) ? x[u][r < R ? r : 0].y : 0.0f;
+          o.y = peer_avg(e, a.world, inv_w);
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r)
-          if (r < a.world) __stcg(reinterpret_cast<float4*>(a.base[r] + i), o);
+          for (int r = 0; r < kMaxPeers; ++r) e[r] = (r < R && r < a.world) ? x[u][r < R ? r : 0].z : 0.0f;
+          o.z = peer_avg(e, a.world, inv_w);
+#pragma unroll
+          for (int r = 0; r < kMaxPeers; ++r) e[r] = (r < R && r < a.world) ? x[u][r < R ? r : 0].w : 0.0f;
+          o.w = peer_avg(e, a.world, inv_w);
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+            if (r < a.world)
+              __stcg(reinterpret_cast<float4*>(a.base[r] + a.offset + c0 + 4 * v), o);
+        }
       }
       tail = c0 + 4 * nv;
     }
@@ -375,8 +389,30 @@ orca_status peer_arena_open(orca_comm* c, float* base, int n_slots, PeerArena** 
   return ORCA_OK;
 }
 
+template <bool kVec, int kU>
+static int peer_blocks_per_sm() {
+  static int v = 0;
+  if (!v) {
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, peer_reduce_kernel<kVec, kU>,
+                                                      kPeerThreads, 0) != cudaSuccess || b < 1)
+      b = 1;
+    v = b;
+  }
+  return v;
+}
+
+template <bool kVec, int kU>
+static void launch_peer_reduce(const PeerArgs& a, int64_t per, int sms, double inv_w,
+                               cudaStream_t stream) {
+  const int64_t want = cdiv(per, 4 * kPeerThreads * kU);
+  const int grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)sms * peer_blocks_per_sm<kVec, kU>(), want));
+  peer_reduce_kernel<kVec, kU><<<grid, kPeerThreads, 0, stream>>>(a, inv_w);
+}
+
 orca_status peer_arena_allreduce_avg(PeerArena* pa, int slot, int64_t offset, int64_t n,
-                                     uint32_t seq, cudaStream_t stream) {
+                                     uint32_t seq, cudaStream_t stream, int sms) {
   if (!pa || slot < 0 || slot >= pa->n_slots || n < 0 || offset < 0)
     return fail(ORCA_INVALID_ARGUMENT, "peer exchange: bad range");
   if (n == 0) return ORCA_OK;
@@ -389,13 +425,18 @@ orca_status peer_arena_allreduce_avg(PeerArena* pa, int slot, int64_t offset, in
   orca_ctx* ctx = pa->comm->ctx;
   peer_signal_kernel<<<1, 32, 0, stream>>>(a, 0);
   const int64_t per = (cdiv(n, (int64_t)a.world) + 3) & ~int64_t(3);
-  const int grid =
-      (int)std::max<int64_t>(1, std::min<int64_t>(ctx->sm_count, cdiv(per, 4 * kPeerThreads)));
   const double inv_w = 1.0 / (double)a.world;
-  if ((offset & 3) == 0)
-    peer_reduce_kernel<true><<<grid, kPeerThreads, 0, stream>>>(a, inv_w);
+  // Grid: as many blocks as fit on `sms` SMs (the SMs the caller leaves free
+  // next to its GEMMs), so that every block runs at once.
+  sms = sms > 0 ? std::min(sms, ctx->sm_count) : ctx->sm_count;
+  if ((offset & 3) != 0)
+    launch_peer_reduce<false, 1>(a, per, sms, inv_w, stream);
+  else if (a.world <= 2)
+    launch_peer_reduce<true, 4>(a, per, sms, inv_w, stream);
+  else if (a.world <= 4)
+    launch_peer_reduce<true, 2>(a, per, sms, inv_w, stream);
   else
-    peer_reduce_kernel<false><<<grid, kPeerThreads, 0, stream>>>(a, inv_w);
+    launch_peer_reduce<true, 1>(a, per, sms, inv_w, stream);
   count_launch(ctx, 2);
   ORCA_CUDA_TRY(cudaGetLastError());
   return ORCA_OK;

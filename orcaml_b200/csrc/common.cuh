@@ -30,7 +30,7 @@ orca_status fail(orca_status s, const char* fmt, ...);
 struct PeerArena;
 orca_status peer_arena_open(orca_comm* c, float* base, int n_slots, PeerArena** out);
 orca_status peer_arena_allreduce_avg(PeerArena* pa, int slot, int64_t offset, int64_t n,
-                                     uint32_t seq, cudaStream_t stream);
+                                     uint32_t seq, cudaStream_t stream, int sms = 0);
 void peer_arena_close(PeerArena* pa);
 // Looks up, once per device, the device address of the fixed scratch array of
 // orca_softmax_ce_fwd_bwd_noalloc (mlp.cu); the device must be current.

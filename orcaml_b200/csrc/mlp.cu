@@ -1450,21 +1450,37 @@ static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad) {
 // the all-reduce 16 or 24 SMs made the GEMM 0.3-0.55 ms slower while the
 // all-reduce, contending for memory with it, still took 1.4-2.1 ms; the step
 // was 1.5-3 % slower than with the GEMM on every SM.
+//
+// With the peer exchange the reservation is on by default (ORCA_PEER_SMS,
+// 16): its kernel moves a layer's gradients at close to NVLink speed from a
+// handful of SMs, so the layer-1 exchange finishes inside the first part of
+// the dX GEMM.  (It cannot share an SM with a GEMM CTA: the GEMM's ten warps
+// at 168 registers leave too few registers on the scheduler partitions.)
 struct CommOverlap {
   int reserve_sms;
   double first_fraction;
 };
-static CommOverlap comm_overlap() {
-  static const CommOverlap v = [] {
-    CommOverlap o{0, 0.5};
-    if (const char* e = getenv("ORCA_COMM_SMS")) o.reserve_sms = std::max(0, atoi(e));
-    if (const char* e = getenv("ORCA_COMM_SPLIT")) {
-      const double f = atof(e);
-      if (f > 0.0 && f < 1.0) o.first_fraction = f;
-    }
-    return o;
-  }();
-  return v;
+static CommOverlap comm_overlap(bool peer) {
+  static const CommOverlap v[2] = {
+      [] {
+        CommOverlap o{0, 0.5};
+        if (const char* e = getenv("ORCA_COMM_SMS")) o.reserve_sms = std::max(0, atoi(e));
+        if (const char* e = getenv("ORCA_COMM_SPLIT")) {
+          const double f = atof(e);
+          if (f > 0.0 && f < 1.0) o.first_fraction = f;
+        }
+        return o;
+      }(),
+      [] {
+        CommOverlap o{16, 0.5};
+        if (const char* e = getenv("ORCA_PEER_SMS")) o.reserve_sms = std::max(0, atoi(e));
+        if (const char* e = getenv("ORCA_COMM_SPLIT")) {
+          const double f = atof(e);
+          if (f > 0.0 && f < 1.0) o.first_fraction = f;
+        }
+        return o;
+      }()};
+  return v[peer ? 1 : 0];
 }
 
 static orca_status launch_layer_allreduce(orca_mlp* m, int l) {
@@ -1476,8 +1492,11 @@ static orca_status launch_layer_allreduce(orca_mlp* m, int l) {
     const int64_t n = m->dims[l] * m->dims[l + 1] + m->dims[l + 1];
     const int pr = prof_open(m, "allreduce_l" + std::to_string(l), 0.0, 4.0 * (double)n, -1,
                              ctx->comm_stream);
+    // Layers whose exchange overlaps a GEMM run on the SMs the GEMM leaves
+    // free; the first layer's runs after the last GEMM, on every SM.
+    const int sms = l > 0 ? comm_overlap(true).reserve_sms : 0;
     ORCA_TRY(peer_arena_allreduce_avg(m->pex, l, m->p_off[2 * l], n, m->pex_seq,
-                                      ctx->comm_stream));
+                                      ctx->comm_stream, sms));
     prof_close(m, pr);
     ORCA_CUDA_TRY(cudaEventRecord(m->ev_reduced[l], ctx->comm_stream));
     return ORCA_OK;
@@ -1585,7 +1604,7 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
     const int dx_path = gemm_select(ctx, B, K, N, ga, wt, ex, m->gemm_path);
     pr = prof_open(m, "gemm_dx_l" + std::to_string(l), 2.0 * B * N * K,
                    4.0 * ((g_lo ? 2 : 1) * B * N + 2 * K * N + 4 * B * K), dx_path);
-    const CommOverlap ov = comm_overlap();
+    const CommOverlap ov = comm_overlap(m->pex != nullptr);
     if (m->comm && dx_path == GEMM_TC && ov.reserve_sms > 0 && ov.reserve_sms < ctx->sm_count) {
       // This layer's gradient all-reduce was just queued on the comm stream.
       // The persistent GEMM would take every SM before the collective's CTAs
