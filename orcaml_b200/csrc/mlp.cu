@@ -1033,7 +1033,7 @@ orca_status orca_mlp_bucket_plan(int n_layers, const int64_t* dims, size_t bucke
 }
 
 // Whether AUTO takes the peer exchange when it can be set up.
-constexpr bool kAutoPeer = false;
+constexpr bool kAutoPeer = true;
 // ORCA_XCHG=nccl|peer overrides the automatic choice (for measurements).
 static int xchg_env() {
   static const int v = [] {
