@@ -445,10 +445,15 @@ def run_ours(args):
         tr.graph_release()
     prof_steps = max(3, min(args.steps, 10))
     tr.profile_begin()
+    p0 = torch.cuda.Event(enable_timing=True)
+    p1 = torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
     for _ in range(prof_steps):
         tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
+    p1.record(stream)
     sites = tr.profile_end()
     barrier()
+    prof_ms_step = p0.elapsed_time(p1) / prof_steps
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_step = ms / args.steps
     value = world * B * args.steps / (ms / 1000.0)
@@ -553,6 +558,9 @@ def run_ours(args):
             "loss": loss_val,
             "breakdown_ms": breakdown,
             "breakdown_note": f"per launch, from {prof_steps} profiled steps after the timed ones",
+            "profiled_ms_per_step": prof_ms_step,
+            "breakdown_sum_ms": sum(s["ms"] for s in sites
+                                    if not s["name"].startswith("allreduce")) / prof_steps,
             "clocks": clocks.summary(),
         }
         if cpu is not None:
