@@ -9,8 +9,9 @@ The default workload is configs[2], the configuration BASELINE's metric is
 quoted on; `--config` runs the other MLP configs the same way (their own
 optimizer, inputs and shapes) for reference measurements.
 
-A step is one full training step (forward, softmax-CE, backward, NCCL
-all-reduce of the gradients when N > 1, optimizer update).  Every rank holds a
+A step is one full training step (forward, softmax-CE, backward, the
+gradient exchange when N > 1 -- the peer-memory kernel by default, NCCL with
+ORCA_XCHG=nccl -- and the optimizer update).  Every rank holds a
 full replica and its own batch (weak scaling); `value` counts samples of all
 ranks.  Timing: W untimed steps, then K steps bracketed by a barrier and a
 device synchronise on both sides, timed with CUDA events on the library's
@@ -19,8 +20,8 @@ weight planes alone are 512 MB) exceeds the 126 MB L2, so no flush is needed.
 
 At N > 1 every rank first runs a data-parallel parity pre-check outside the
 timed region (`ddp_parity` in the JSON line; `--no-parity` skips it): a
-reduced model through the same trainer and NCCL communicator, against the
-oracle's restatement of the reference's DDP average.
+reduced model through the same trainer, communicator and exchange, against
+the oracle's restatement of the reference's DDP average.
 
 `--impl reference` times the reference's CPU path restated in oracle/ (the
 Rust reference cannot be built here) on the host cores, rank 0 only, with a
@@ -113,6 +114,14 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def wait_first(self, limit_s=5.0):
+        """Blocks until the first sample has arrived (nvidia-smi takes a
+        moment to start, longer with eight processes starting it at once), so
+        that a short timed region is still sampled; at most limit_s."""
+        t0 = time.perf_counter()
+        while self.proc is not None and not self.lines and time.perf_counter() - t0 < limit_s:
+            time.sleep(0.01)
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -423,6 +432,7 @@ def run_ours(args):
             tr.step_device(xs.device_ptr, ts.device_ptr, loss_s.device_ptr)
 
     clocks = ClockSampler(local).__enter__()   # sampling from warm-up on
+    clocks.wait_first()
     for _ in range(args.warmup):
         device_step()
     barrier()
