@@ -572,6 +572,8 @@ struct orca_mlp {
   float* x_stage = nullptr;          // raw input [B][dims[0]]
   float* logits = nullptr;           // [B][C]
   float* dlogits = nullptr;          // [B][C]
+  float* dlogit_planes = nullptr;    // [2][B][C]: dlogits split for the classifier's products
+                                     // when they run as GEMMs (no classifier fusion)
   float* row_loss = nullptr;         // [B]
   float* loss = nullptr;             // [1]
   float* dz[2] = {nullptr, nullptr}; // ping-pong (hi, lo) planes of hidden-layer dZ
@@ -820,6 +822,10 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
   if (cudaMallocHost(reinterpret_cast<void**>(&m->host_stage), 2 * sizeof(float)) != cudaSuccess)
     return cleanup(fail(ORCA_CUDA_ERROR, "pinned host allocation failed"));
   m->use_head = L >= 2 && C <= HEAD_MAX_CLASSES && m->gemm_path != GEMM_SIMT;
+  // Without the fused classifier pass, the classifier's dW and dX products
+  // take dlogits as an operand; split into planes they can run on the tensor
+  // cores (plain fp32 would send them to the FFMA kernels).
+  if (!m->use_head) ALLOC(dlogit_planes, (size_t)(2 * B * C) * 4);
   if (m->use_head) {
     const int64_t H = m->dims[L - 1];
     m->head_ldp = (C + 3) / 4 * 4;
@@ -1527,6 +1533,15 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
   const float* g_hi = m->dlogits;
   const float* g_lo = nullptr;
   int64_t g_ld = m->dims[L];
+  if (m->dlogit_planes) {
+    // hi + lo == dlogits exactly, so every path computes the same products.
+    const int64_t n = B * m->dims[L];
+    const int pr = prof_open(m, "split_dlogits", 0.0, 12.0 * n);
+    ORCA_TRY(split_planes(ctx, m->dlogits, m->dlogit_planes, m->dlogit_planes + n, n));
+    prof_close(m, pr);
+    g_hi = m->dlogit_planes;
+    g_lo = m->dlogit_planes + n;
+  }
   int cur = 0;
   for (int l = L - 1; l >= 0; --l) {
     const int64_t K = m->dims[l], N = m->dims[l + 1];
