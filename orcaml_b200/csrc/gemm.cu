@@ -468,24 +468,33 @@ __device__ __forceinline__ void load_operand_pair(uint8_t* dst, const CUtensorMa
 // epilogue (and, with kDot, adds their next-layer dot into part).  Q is a
 // template parameter so that every accumulator index is a compile-time
 // constant and the array stays in registers.
-template <int Q, bool kDot>
+template <int Q, bool kDot, bool kBits>
 __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, int64_t N, int64_t m,
                                                int64_t n0, const float (&acc)[128], uint32_t part) {
 #define v(i) acc[Q * 32 + (i)]
   if (m >= M) return;
   const bool full = (n0 + 32 <= N) && ((ep.ldc & 3) == 0);
+  // This thread owns columns [n0, n0 + 32) of row m: one word of ReLU bits.
+  const int64_t bit_word = m * ep.bits_ld + n0 / 32;
   if (!full) {
+    // Edge tiles: element by element; a mask comes from the planes (which the
+    // caller always provides with EPI_MASK_SPLIT), bits are still written.
+    uint32_t bits = 0;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (n0 + j < N) {
         store_epi(ep, m, n0 + j, v(j));
-        if (kDot) {
+        if (kDot || (kBits && ep.relu_bits_out && ep.mode == EPI_BIAS_RELU_SPLIT)) {
           const float y = __fadd_rn(v(j), ep.bias[n0 + j]);
-          const float a1[1] = {y > 0.0f ? y : 0.0f};
-          dot_group<1>(ep, n0 + j, a1, part);
+          if (y > 0.0f) bits |= 1u << j;
+          if (kDot) {
+            const float a1[1] = {y > 0.0f ? y : 0.0f};
+            dot_group<1>(ep, n0 + j, a1, part);
+          }
         }
       }
     }
+    if (kBits && ep.relu_bits_out && ep.mode == EPI_BIAS_RELU_SPLIT) ep.relu_bits_out[bit_word] = bits;
     return;
   }
   const int64_t base = m * ep.ldc + n0;
@@ -511,6 +520,9 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
   float4* ol = reinterpret_cast<float4*>(ep.out_lo + base);
   const float4* mh = reinterpret_cast<const float4*>(ep.mask_hi + base);
   const float4* ml = reinterpret_cast<const float4*>(ep.mask_lo + base);
+  const uint32_t in_bits =
+      (kBits && ep.mode == EPI_MASK_SPLIT && ep.relu_bits) ? ep.relu_bits[bit_word] : 0u;
+  uint32_t out_bits = 0;
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     float x[4] = {v(4 * q + 0), v(4 * q + 1), v(4 * q + 2), v(4 * q + 3)};
@@ -518,15 +530,22 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float y = __fadd_rn(x[e], ep.bias[n0 + 4 * q + e]);
+        if (kBits && y > 0.0f) out_bits |= 1u << (4 * q + e);
         x[e] = y > 0.0f ? y : 0.0f;
       }
       if (kDot) dot_group<4>(ep, n0 + 4 * q, x, part);
     } else if (ep.mode == EPI_MASK_SPLIT) {
-      float4 a = mh[q], b = ml[q];
-      x[0] = __fadd_rn(a.x, b.x) > 0.0f ? x[0] : 0.0f;
-      x[1] = __fadd_rn(a.y, b.y) > 0.0f ? x[1] : 0.0f;
-      x[2] = __fadd_rn(a.z, b.z) > 0.0f ? x[2] : 0.0f;
-      x[3] = __fadd_rn(a.w, b.w) > 0.0f ? x[3] : 0.0f;
+      if (kBits && ep.relu_bits) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (!((in_bits >> (4 * q + e)) & 1u)) x[e] = 0.0f;
+      } else {
+        float4 a = mh[q], b = ml[q];
+        x[0] = __fadd_rn(a.x, b.x) > 0.0f ? x[0] : 0.0f;
+        x[1] = __fadd_rn(a.y, b.y) > 0.0f ? x[1] : 0.0f;
+        x[2] = __fadd_rn(a.z, b.z) > 0.0f ? x[2] : 0.0f;
+        x[3] = __fadd_rn(a.w, b.w) > 0.0f ? x[3] : 0.0f;
+      }
     }
     float4 h, l;
     split_tf32(x[0], h.x, l.x);
@@ -541,10 +560,11 @@ __device__ __forceinline__ void epilogue_chunk(const Epilogue& ep, int64_t M, in
       ol[q] = l;
     }
   }
+  if (kBits && ep.relu_bits_out && ep.mode == EPI_BIAS_RELU_SPLIT) ep.relu_bits_out[bit_word] = out_bits;
 }
 #undef v
 
-template <bool kDot>
+template <bool kDot, bool kBits>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                const Params p) {
@@ -757,10 +777,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
         for (int q = 0; q < 4; ++q) sts128(part + 16 * q, make_float4(0.f, 0.f, 0.f, 0.f));
       }
-      if (nb < p.N) epilogue_chunk<0, kDot>(p.ep, p.M, p.N, m, nb, acc, part);
-      if (nb + 32 < p.N) epilogue_chunk<1, kDot>(p.ep, p.M, p.N, m, nb + 32, acc, part);
-      if (nb + 64 < p.N) epilogue_chunk<2, kDot>(p.ep, p.M, p.N, m, nb + 64, acc, part);
-      if (nb + 96 < p.N) epilogue_chunk<3, kDot>(p.ep, p.M, p.N, m, nb + 96, acc, part);
+      if (nb < p.N) epilogue_chunk<0, kDot, kBits>(p.ep, p.M, p.N, m, nb, acc, part);
+      if (nb + 32 < p.N) epilogue_chunk<1, kDot, kBits>(p.ep, p.M, p.N, m, nb + 32, acc, part);
+      if (nb + 64 < p.N) epilogue_chunk<2, kDot, kBits>(p.ep, p.M, p.N, m, nb + 64, acc, part);
+      if (nb + 96 < p.N) epilogue_chunk<3, kDot, kBits>(p.ep, p.M, p.N, m, nb + 96, acc, part);
       if (kDot && m < p.M && nb < p.N) {
         // BN is a multiple of DOT_SLICE: nb / DOT_SLICE is this half-tile's slice.
         float* o = p.ep.dot_out + ((nb / DOT_SLICE) * p.M + m) * p.ep.dot_ldp;
@@ -817,7 +837,7 @@ constexpr int PB_STAGE = 2 * PB_ROWS * BK * 4;       // 16 KB
 static_assert(PSTAGES * (PA_STAGE + PB_STAGE) == TILE_BYTES, "same stage budget as tc_gemm_kernel");
 static_assert(2 * PSTAGES + 5 <= 30, "barriers fit in the 256-byte barrier area");
 
-template <bool kDot>
+template <bool kDot, bool kBits>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                     const __grid_constant__ CUtensorMap map_b, const Params p) {
@@ -1028,10 +1048,10 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
 #pragma unroll
         for (int q = 0; q < 4; ++q) sts128(part + 16 * q, make_float4(0.f, 0.f, 0.f, 0.f));
       }
-      if (nb < p.N) epilogue_chunk<0, kDot>(p.ep, p.M, p.N, m, nb, acc, part);
-      if (nb + 32 < p.N) epilogue_chunk<1, kDot>(p.ep, p.M, p.N, m, nb + 32, acc, part);
-      if (nb + 64 < p.N) epilogue_chunk<2, kDot>(p.ep, p.M, p.N, m, nb + 64, acc, part);
-      if (nb + 96 < p.N) epilogue_chunk<3, kDot>(p.ep, p.M, p.N, m, nb + 96, acc, part);
+      if (nb < p.N) epilogue_chunk<0, kDot, kBits>(p.ep, p.M, p.N, m, nb, acc, part);
+      if (nb + 32 < p.N) epilogue_chunk<1, kDot, kBits>(p.ep, p.M, p.N, m, nb + 32, acc, part);
+      if (nb + 64 < p.N) epilogue_chunk<2, kDot, kBits>(p.ep, p.M, p.N, m, nb + 64, acc, part);
+      if (nb + 96 < p.N) epilogue_chunk<3, kDot, kBits>(p.ep, p.M, p.N, m, nb + 96, acc, part);
       if (kDot && m < p.M && nb < p.N) {
         float* o = p.ep.dot_out + ((nb / DOT_SLICE) * p.M + m) * p.ep.dot_ldp;
         float sv[16];
@@ -1167,7 +1187,7 @@ static int pair_policy() {
 }
 
 // Most clusters of two CTAs of a pair kernel that fit on the device at once.
-template <bool kDot>
+template <bool kDot, bool kBits>
 static orca_status pair_clusters(orca_ctx* ctx, int* out) {
   static int cached[64] = {};
   if (ctx->device < 64 && cached[ctx->device] > 0) {
@@ -1186,18 +1206,18 @@ static orca_status pair_clusters(orca_ctx* ctx, int* out) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  ORCA_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, tc_gemm_pair_kernel<kDot>, &cfg));
+  ORCA_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, tc_gemm_pair_kernel<kDot, kBits>, &cfg));
   if (n < 1) return fail(ORCA_CUDA_ERROR, "no cluster of two CTAs fits on the device");
   if (ctx->device < 64) cached[ctx->device] = n;
   *out = n;
   return ORCA_OK;
 }
 
-template <bool kDot>
+template <bool kDot, bool kBits>
 static orca_status launch_pair(orca_ctx* ctx, const CUtensorMap& ma, const CUtensorMap& mb,
                                const Params& p, int64_t tiles) {
   int nclusters = 0;
-  ORCA_TRY(pair_clusters<kDot>(ctx, &nclusters));
+  ORCA_TRY((pair_clusters<kDot, kBits>(ctx, &nclusters)));
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1210,7 +1230,7 @@ static orca_status launch_pair(orca_ctx* ctx, const CUtensorMap& ma, const CUten
   cfg.stream = ctx->stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  ORCA_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<kDot>, ma, mb, p));
+  ORCA_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<kDot, kBits>, ma, mb, p));
   return ORCA_OK;
 }
 
@@ -1218,16 +1238,15 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
                    const Operand& B, const Epilogue& ep, int path, const TileRange* range) {
   static bool attr_set[64] = {};
   if (ctx->device < 64 && !attr_set[ctx->device]) {
-    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES_DOT));
-    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_pair_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    ORCA_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_pair_kernel<true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES_DOT));
+    const auto smem_attr = [](const void* fn, int bytes) {
+      return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    };
+    ORCA_CUDA_TRY(smem_attr((const void*)tc_gemm_kernel<false, false>, SMEM_BYTES));
+    ORCA_CUDA_TRY(smem_attr((const void*)tc_gemm_kernel<false, true>, SMEM_BYTES));
+    ORCA_CUDA_TRY(smem_attr((const void*)tc_gemm_kernel<true, false>, SMEM_BYTES_DOT));
+    ORCA_CUDA_TRY(smem_attr((const void*)tc_gemm_pair_kernel<false, false>, SMEM_BYTES));
+    ORCA_CUDA_TRY(smem_attr((const void*)tc_gemm_pair_kernel<false, true>, SMEM_BYTES));
+    ORCA_CUDA_TRY(smem_attr((const void*)tc_gemm_pair_kernel<true, false>, SMEM_BYTES_DOT));
     attr_set[ctx->device] = true;
   }
   const int policy = pair_policy();
@@ -1306,16 +1325,25 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
   static_assert(BN % DOT_SLICE == 0 && DOT_SLICE == 128, "one dot slice per epilogue half");
   static_assert(EPI_WARPS == 8 && HEAD_MAX_CLASSES == 16 && SMEM_BYTES_DOT <= 232448,
                 "dot slots: 256 epilogue threads x DOT_SLOT floats");
+  // ReLU bits are written or read only by the kernels compiled for them (the
+  // next-layer dot and the bits never meet: the dot's activation feeds the
+  // classifier pass, not a dX product).
+  const bool bits = !ep.dot_out && (ep.relu_bits_out || ep.relu_bits);
   if (pair) {
     const int64_t pair_tiles = cdiv(M, 2 * BM) * cdiv(N, BN);
-    if (ep.dot_out) ORCA_TRY(launch_pair<true>(ctx, ma, mb, p, pair_tiles));
-    else ORCA_TRY(launch_pair<false>(ctx, ma, mb, p, pair_tiles));
+    if (ep.dot_out) ORCA_TRY((launch_pair<true, false>(ctx, ma, mb, p, pair_tiles)));
+    else if (bits) ORCA_TRY((launch_pair<false, true>(ctx, ma, mb, p, pair_tiles)));
+    else ORCA_TRY((launch_pair<false, false>(ctx, ma, mb, p, pair_tiles)));
     count_launch(ctx);
     return ORCA_OK;
   }
   ORCA_CUDA_TRY(cudaMemsetAsync(ctx->tile_ctr, 0, sizeof(int), ctx->stream));
-  if (ep.dot_out) tc_gemm_kernel<true><<<grid, THREADS, SMEM_BYTES_DOT, ctx->stream>>>(ma, mb, p);
-  else tc_gemm_kernel<false><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
+  if (ep.dot_out)
+    tc_gemm_kernel<true, false><<<grid, THREADS, SMEM_BYTES_DOT, ctx->stream>>>(ma, mb, p);
+  else if (bits)
+    tc_gemm_kernel<false, true><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
+  else
+    tc_gemm_kernel<false, false><<<grid, THREADS, SMEM_BYTES, ctx->stream>>>(ma, mb, p);
   count_launch(ctx);
   ORCA_CUDA_TRY(cudaGetLastError());
   return ORCA_OK;

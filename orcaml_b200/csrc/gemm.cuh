@@ -35,6 +35,15 @@ struct Epilogue {
   const float* bias = nullptr;
   const float* mask_hi = nullptr;   // same [M, ldc] layout as out
   const float* mask_lo = nullptr;
+  // ReLU decisions as bits, word [m * bits_ld + n / 32] bit n % 32 = (value at
+  // (m, n) > 0), on the tensor-core path only: EPI_BIAS_RELU_SPLIT writes them
+  // to relu_bits_out when it is set; EPI_MASK_SPLIT reads its mask from
+  // relu_bits when it is set (4 bytes per 32 columns instead of both mask
+  // planes, 8 bytes per element) in full 32-column groups; edge groups and
+  // the other paths read the mask planes, which EPI_MASK_SPLIT always needs.
+  uint32_t* relu_bits_out = nullptr;
+  const uint32_t* relu_bits = nullptr;
+  int64_t bits_ld = 0;
   // Next-layer dot (EPI_BIAS_RELU_SPLIT on the tensor-core path only): the
   // activation a[m, n] also feeds the classifier layer's product.  Slice s of
   // 128 output columns writes, for j < dot_n (<= 16),

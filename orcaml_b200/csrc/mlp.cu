@@ -568,6 +568,11 @@ struct orca_mlp {
   float* x_planes = nullptr;         // [2][B][x_ld]: input planes + a column of ones
   int64_t x_ld = 0;                  // dims[0] + 1 rounded up to a multiple of 4
   std::vector<float*> act_planes;    // act_planes[l] = [2][B][dims[l]], l = 1..L-1
+  // ReLU decisions of act[l] as bits ([B][ceil(dims[l] / 32)] words), written by
+  // the forward GEMM's epilogue and read by the dX GEMM's mask epilogue when
+  // both run on the tensor cores; relu_bits_ok[l]: this step's forward wrote them.
+  std::vector<uint32_t*> relu_bits;
+  std::vector<char> relu_bits_ok;
   float* t_buf = nullptr;            // one-hot target [B][C]
   float* x_stage = nullptr;          // raw input [B][dims[0]]
   float* logits = nullptr;           // [B][C]
@@ -806,9 +811,15 @@ orca_status orca_mlp_create(orca_ctx* ctx, const orca_mlp_config* cfg, orca_mlp*
   ALLOC(row_loss, (size_t)B * 4);
   ALLOC(loss, 64);
   m->act_planes.assign(L, nullptr);
+  m->relu_bits.assign(L, nullptr);
+  m->relu_bits_ok.assign(L, 0);
   int64_t maxh = 1;
   for (int l = 1; l < L; ++l) {
     ALLOC(act_planes[l], (size_t)(2 * B * m->dims[l]) * 4);
+    void* pb = nullptr;
+    orca_status sb = mlp_alloc(m, &pb, (size_t)(B * cdiv(m->dims[l], 32)) * 4);
+    if (sb != ORCA_OK) return cleanup(sb);
+    m->relu_bits[l] = static_cast<uint32_t*>(pb);
     maxh = std::max(maxh, m->dims[l]);
   }
   m->dz_plane = B * maxh;
@@ -1425,6 +1436,19 @@ static orca_status mlp_forward_impl(orca_mlp* m, bool with_loss_grad) {
       }
     }
     const int path = gemm_select(ctx, B, N, K, a, w, ep, m->gemm_path);
+    // The ReLU decisions as bits for the dX product of layer l + 1 (not for
+    // the classifier pass, which reads the activation itself).
+    if (l + 1 < L) {
+      // ORCA_RELU_BITS=0 keeps the dX masks on the activation planes.
+      static const bool bits_on = [] {
+        const char* e = getenv("ORCA_RELU_BITS");
+        return !(e && e[0] == '0');
+      }();
+      const bool bits = bits_on && path == GEMM_TC && !(m->use_head && l + 1 == L - 1);
+      ep.relu_bits_out = bits ? m->relu_bits[l + 1] : nullptr;
+      ep.bits_ld = cdiv(N, 32);
+      m->relu_bits_ok[l + 1] = bits ? 1 : 0;
+    }
     const int pr = prof_open(m, "gemm_fwd_l" + std::to_string(l), 2.0 * B * N * K,
                              4.0 * (2 * B * K + 2 * K * N + (l + 1 < L ? 2 : 1) * B * N), path);
     ORCA_TRY(gemm(ctx, B, N, K, a, w, ep, m->gemm_path, m->workspace, m->workspace_bytes));
@@ -1617,6 +1641,10 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
     ex.mask_hi = m->act_planes[l];
     ex.mask_lo = m->act_planes[l] + B * K;
     const int dx_path = gemm_select(ctx, B, K, N, ga, wt, ex, m->gemm_path);
+    if (dx_path == GEMM_TC && m->relu_bits_ok[l]) {
+      ex.relu_bits = m->relu_bits[l];
+      ex.bits_ld = cdiv(K, 32);
+    }
     pr = prof_open(m, "gemm_dx_l" + std::to_string(l), 2.0 * B * N * K,
                    4.0 * ((g_lo ? 2 : 1) * B * N + 2 * K * N + 4 * B * K), dx_path);
     const CommOverlap ov = comm_overlap(m->pex != nullptr);
