@@ -321,6 +321,7 @@ struct Params {
   int64_t M, N, K;
   int a_mn, b_mn;
   int chunk_kb;            // k-blocks per accumulation chunk (>= 1)
+  int head_kb;             // ... of each of a tile's first two chunks (>= chunk_kb)
   Epilogue ep;
   int* dev_err;
   int* tile_ctr;           // zeroed before each launch of tc_gemm_kernel
@@ -329,6 +330,15 @@ struct Params {
   int group_m;             // tile rows per raster group (consecutive tiles share B columns)
   int load_evict_last;     // operand loads carry an L2 evict-last policy
 };
+
+// Chunk c of a tile holds `head` k-blocks for c < 2 and `f` after that (the
+// last chunk ends at the tile's last k-block).  The MMA warp and the
+// epilogue warps agree on the schedule through these two functions.
+__host__ __device__ inline int chunk_len(int c, int head, int f) { return c < 2 ? head : f; }
+__host__ __device__ inline int tile_chunks(int nk, int head, int f) {
+  if (nk <= 2 * head) return (nk + head - 1) / head;
+  return 2 + (nk - 2 * head + f - 1) / f;
+}
 
 // Dynamic tile scheduling of tc_gemm_kernel: the producer takes the next tile
 // index from a global counter and hands it to the MMA warp and the epilogue
@@ -671,6 +681,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       uint32_t chunk_ctr = 0;             // chunks issued so far (all tiles)
       bool ok = true;
       const int F = p.chunk_kb;
+      const int H = p.head_kb;
       const int nk32 = (int)nk;
       for (uint32_t tq_i = 0; ok; ++tq_i) {
         const int slot = (int)(tq_i % TQ);
@@ -684,6 +695,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         uint32_t d_tmem = tmem_base;
         int buf = 0;
         int in_chunk = 0;                 // k-blocks issued into the current chunk
+        int chunk_in_tile = 0;            // chunks of this tile issued so far
         for (int kb = 0; kb < nk32; ++kb) {
           const bool chunk_start = in_chunk == 0;
           if (chunk_start) {
@@ -713,9 +725,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
           tc_commit(&empty_bar[stage]);   // frees the smem stage once these MMAs finish
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
-          if (++in_chunk == F || kb == nk32 - 1) {
+          if (++in_chunk == chunk_len(chunk_in_tile, H, F) || kb == nk32 - 1) {
             tc_commit(&tfull_bar[buf]);   // chunk ready for the epilogue
             ++chunk_ctr;
+            ++chunk_in_tile;
             in_chunk = 0;
           }
         }
@@ -732,7 +745,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     // rule) and columns [128*half, +128) of the 256-column tile.
     const int quarter = warp & 3;
     const int half = (warp - 2) / 4;
-    const int nchunks = (int)cdiv(nk, p.chunk_kb);
+    const int nchunks = tile_chunks((int)nk, p.head_kb, p.chunk_kb);
     uint32_t chunk_ctr = 0;
     bool ok = true;
     for (uint32_t tq_i = 0; ok; ++tq_i) {
@@ -957,11 +970,13 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
       uint32_t chunk_ctr = 0;
       bool ok = true;
       const int F = p.chunk_kb;
+      const int H = p.head_kb;
       const int nk32 = (int)nk;
       for (int64_t tile = cluster; tile < num_tiles && ok; tile += nclusters) {
         uint32_t d_tmem = tmem_base;
         int buf = 0;
         int in_chunk = 0;
+        int chunk_in_tile = 0;
         for (int kb = 0; kb < nk32; ++kb) {
           const bool chunk_start = in_chunk == 0;
           if (chunk_start) {
@@ -992,10 +1007,11 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
           tc_commit_pair(cluster_addr(&empty_bar[stage], 0));
           tc_commit_pair(cluster_addr(&empty_bar[stage], 1));
           if (++stage == PSTAGES) { stage = 0; phase ^= 1u; }
-          if (++in_chunk == F || kb == nk32 - 1) {
+          if (++in_chunk == chunk_len(chunk_in_tile, H, F) || kb == nk32 - 1) {
             tc_commit_pair(cluster_addr(&tfull_bar[buf], 0));
             tc_commit_pair(cluster_addr(&tfull_bar[buf], 1));
             ++chunk_ctr;
+            ++chunk_in_tile;
             in_chunk = 0;
           }
         }
@@ -1010,7 +1026,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
     // ------------------------------------------------------------ epilogue (both)
     const int quarter = warp & 3;
     const int half = (warp - 2) / 4;
-    const int nchunks = (int)cdiv(nk, p.chunk_kb);
+    const int nchunks = tile_chunks((int)nk, p.head_kb, p.chunk_kb);
     const uint32_t tempty_even[2] = {cluster_addr(&tempty_bar[0], 0),
                                      cluster_addr(&tempty_bar[1], 0)};
     uint32_t chunk_ctr = 0;
@@ -1303,14 +1319,29 @@ orca_status launch(orca_ctx* ctx, int64_t M, int64_t N, int64_t K, const Operand
     p.load_evict_last = ((l2hint & 1) && opnd < 96e6) ? 1 : 0;
     p.ep.store_evict_first = (l2hint & 2) ? 1 : 0;
   }
-  // Measured on B200 (mean |error| / sum|a*b|, relu-activation x weight data):
-  // 8 k-blocks per chunk gives 1.6e-8 at K = 8192 and 5e-8 at K = 784, 4 gives
-  // 2.6e-8 at K = 784; a single chain gives 1.0e-6 at K = 8192.  Serial FP32
-  // FFMA gives ~2e-8.  The chunk drains cost ~4% of GEMM time at 8.
+  // Measured on B200 (mean |error| / sum|a*b|, ReLU-activation x weight data,
+  // serial FP32 ~2.0e-8): at K = 8192, chunks of 4 / 8 / 16 / 32 / 49 k-blocks
+  // give 0.9 / 1.8 / 3.4 / 6.9 / 10.3e-8 (a single chain: 1.0e-6); at K = 784,
+  // 4 gives 2.8e-8 and 8 5.4e-8.  Each chunk boundary costs the MMA time (the
+  // configs[2] step: 8.29-8.31 ms at 8, 8.06-8.10 at 16, 7.97-8.00 at 32), but
+  // at 16 the step's loss already leaves the 1e-6 band around the oracle's in
+  // the teacher-forced parity tests, so long-K products take 8 and short-K 4.
   const int64_t nk = cdiv(K, BK);
   const int64_t want = getenv("ORCA_GEMM_CHUNK_KB") ? chunk_kblocks()
                        : (nk <= 64 ? SHORT_K_CHUNK_KB : DEFAULT_CHUNK_KB);
   p.chunk_kb = (int)std::max<int64_t>(1, std::min<int64_t>(nk, want));
+  // ORCA_GEMM_HEAD_KB = h makes the first two chunks of every tile h k-blocks
+  // long: those are what the MMA can run into while the epilogue warps finish
+  // the previous tile.  Off by default: at K = 8192 with chunk 8, h = 16 / 24 /
+  // 32 gave 1.9 / 2.3 / 2.9e-8 and a 1.3-1.7 % faster configs[2] step, but the
+  // larger errors move the step's loss away from the oracle's by more than
+  // the parity tests allow (chunks of 16 throughout: 1.8e-6 relative on the
+  // loss of a teacher-forced configs[1] step against a 1e-6 bound).
+  static const int head_env = [] {
+    const char* e = getenv("ORCA_GEMM_HEAD_KB");
+    return e ? (int)strtol(e, nullptr, 10) : 0;
+  }();
+  p.head_kb = (int)std::max<int64_t>(p.chunk_kb, std::min<int64_t>(nk, head_env));
   const int64_t tiles = cdiv(M, BM) * cdiv(N, BN);
   p.tile_begin = 0;
   p.tile_end = tiles;

@@ -148,3 +148,22 @@ def test_linear_bwd_fused(be, m, k, n, with_mask):
         assert np.all(np.abs(got_dx - ref) <= 1e-5 * scale + 1e-30)
     _, dw2, _ = be.linear_bwd(up(x), up(w), up(dy), m, k, n, need_dx=False)
     assert np.array_equal(be.to_f32_vec(dw2), be.to_f32_vec(dw))
+
+
+@pytest.mark.parametrize("k,mean_bound", [(8192, 2.5e-8), (784, 3.5e-8)])
+def test_tcgen05_mean_error_at_fp32_level(be, k, mean_bound):
+    """The chunked accumulation keeps the tensor-core product at FP32 accuracy
+    on the data the step multiplies (ReLU activations x Kaiming-scaled
+    weights): mean |C - exact| / sum|a*b| within 1.25x (K = 8192) and 1.75x
+    (K = 784) of a serial k-ascending FP32 sum (about 2e-8 here)."""
+    rng = np.random.default_rng(7)
+    m = n = 256
+    a = np.maximum(rng.standard_normal((m, k)), 0).astype(np.float32)
+    b = (rng.standard_normal((k, n)) * np.sqrt(2.0 / k)).astype(np.float32)
+    sa = be.from_f32_slice([a.size], a)
+    sb = be.from_f32_slice([b.size], b)
+    c = be.to_f32_vec(be.gemm_ex(m, n, k, sa, False, sb, True, 2)).reshape(m, n)
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    scale = np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64)
+    rel = np.abs(c.astype(np.float64) - exact) / scale
+    assert float(rel.mean()) <= mean_bound, float(rel.mean())
