@@ -1645,8 +1645,10 @@ static orca_status mlp_backward_impl(orca_mlp* m) {
       ex.relu_bits = m->relu_bits[l];
       ex.bits_ld = cdiv(K, 32);
     }
+    // Bytes: g, W (both planes), the mask (planes or bits) and dZ (planes).
+    const double mask_bytes = ex.relu_bits ? 4.0 * B * cdiv(K, 32) : 8.0 * B * K;
     pr = prof_open(m, "gemm_dx_l" + std::to_string(l), 2.0 * B * N * K,
-                   4.0 * ((g_lo ? 2 : 1) * B * N + 2 * K * N + 4 * B * K), dx_path);
+                   4.0 * ((g_lo ? 2 : 1) * B * N + 2 * K * N + 2 * B * K) + mask_bytes, dx_path);
     const CommOverlap ov = comm_overlap(m->pex != nullptr);
     if (m->comm && dx_path == GEMM_TC && ov.reserve_sms > 0 && ov.reserve_sms < ctx->sm_count) {
       // This layer's gradient all-reduce was just queued on the comm stream.
